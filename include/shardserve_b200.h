@@ -1,0 +1,141 @@
+/*
+ * shardserve_b200 — C ABI of the B200 (sm_100a) ragged paged-attention hot path.
+ *
+ * Two device operations replace the two halves of the ShardServe attention path:
+ *
+ *   ss_kv_append               replaces Cache.write            (shardserve/cache.py:47-49)
+ *   ss_ragged_paged_attention  replaces ragged_attention_direct (shardserve/kernel.py:11-82)
+ *                              and its Triton kernel           (shardserve/kernel.py:85-166)
+ *
+ * Every entry point takes plain device pointers, element strides and sizes; nothing here
+ * depends on PyTorch. Strides are in ELEMENTS (not bytes), exactly like torch's
+ * Tensor.stride(), which the reference passes to its kernel (kernel.py:61-76).
+ * `stream` is a cudaStream_t passed as void* (NULL = legacy default stream). No entry point
+ * allocates device memory, synchronises the stream or reads device memory on the host, so
+ * all of them can be recorded into a CUDA graph (the reference captures the attention
+ * call in runtime.py:68-71).
+ *
+ * Return value: SS_OK (0) or one of the SS_ERR_* codes; ss_last_error_message() gives a
+ * human-readable reason for the last failure on the calling thread.
+ *
+ * Device-side problems that the host cannot see without reading device memory (a page id
+ * outside the pool, a sequence id outside the block table, a position past the block-table
+ * width, an append slot outside the pool) never fault: the offending page reads as zeros
+ * (attention) or the row is skipped (append), and a bit is OR-ed into the 32-bit error word
+ * at byte offset 0 of the workspace (SS_DEVERR_* below). ss_fetch_device_errors() reads it.
+ */
+#ifndef SHARDSERVE_B200_H
+#define SHARDSERVE_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#if defined(__GNUC__)
+#define SS_API __attribute__((visibility("default")))
+#else
+#define SS_API
+#endif
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* ---- status codes ---------------------------------------------------------------------- */
+#define SS_OK 0
+#define SS_ERR_INVALID 1     /* bad argument: shape, dtype flag, null pointer, stride      */
+#define SS_ERR_UNSUPPORTED 2 /* valid for the reference but not for this build (none today) */
+#define SS_ERR_CUDA 3        /* a CUDA runtime call failed                                  */
+#define SS_ERR_WORKSPACE 4   /* workspace missing or smaller than ss_attention_workspace_bytes */
+
+/* ---- device error bits (OR-ed into the workspace error word) --------------------------- */
+#define SS_DEVERR_PAGE 0x1u     /* block-table entry outside [0, num_pages)              */
+#define SS_DEVERR_SEQ 0x2u      /* query_seq_ids entry outside [0, block_table rows)     */
+#define SS_DEVERR_POS 0x4u      /* position < 0 or position + 1 > 16 * block_table cols   */
+#define SS_DEVERR_SLOT 0x8u     /* append slot outside [0, 16 * num_pages)               */
+#define SS_DEVERR_TIMEOUT 0x10u /* a bounded on-chip wait gave up (never expected)        */
+
+/* Page size of the paged pool: the reference supports exactly 16 (kernel.py:8, 36-37). */
+#define SS_BLOCK_SIZE 16
+
+/* Library version (major * 10000 + minor * 100 + patch). */
+SS_API int ss_version(void);
+
+/* Text for a status code; never NULL. */
+SS_API const char* ss_status_string(int status);
+
+/* Reason for the last non-OK return on the calling thread ("" if none). */
+SS_API const char* ss_last_error_message(void);
+
+/*
+ * Slot-mapped KV append.  Replaces Cache.write (shardserve/cache.py:47-49):
+ *     k_pool.flatten(0, 1)[slots[i]] = k[i];  v_pool.flatten(0, 1)[slots[i]] = v[i]
+ * k, v        : bf16 [tokens, kv_heads, head_dim]   (strides k_strides / v_strides)
+ * k_pool/v_pool: bf16 [num_pages, 16, kv_heads, head_dim] (strides *_pool_strides)
+ * slots       : [tokens] int32 (slots_is_int64 = 0) or int64 (= 1); slot s is row s % 16 of
+ *               page s / 16 (the reference builds s = table[p // 16] * 16 + p % 16,
+ *               runtime.py:38).
+ * workspace   : optional (may be NULL); if given, its error word receives SS_DEVERR_SLOT.
+ * Copies are bit-exact.  Slots outside the pool are skipped.  Duplicate slots within one
+ * call leave one of the candidate rows, unspecified which (as index_copy_ does).
+ */
+SS_API int ss_kv_append(const void* k, const int64_t k_strides[3], const void* v,
+                 const int64_t v_strides[3], void* k_pool, const int64_t k_pool_strides[4],
+                 void* v_pool, const int64_t v_pool_strides[4], const void* slots,
+                 int slots_is_int64, int64_t tokens, int64_t num_pages, int kv_heads,
+                 int head_dim, void* workspace, void* stream);
+
+/*
+ * Workspace size (bytes) that ss_ragged_paged_attention needs on `device` for this geometry.
+ * The workspace must be ZERO-FILLED before its first use; every call that completes leaves
+ * it ready for the next call (split-K tickets are reset by the CTA that consumes them), so
+ * one buffer can be reused across calls on one stream.  Calls that run concurrently on
+ * different streams need different workspaces.
+ */
+SS_API int ss_attention_workspace_bytes(int device, int64_t tokens, int heads, int kv_heads,
+                                 int head_dim, size_t* bytes);
+
+/*
+ * Ragged paged attention over a flat batch of query tokens.  Replaces
+ * ragged_attention_direct(q, k_pool_layer, v_pool_layer, block_tables, query_seq_ids,
+ * positions, sm_scale) (shardserve/kernel.py:11-82) and its kernel (kernel.py:85-166):
+ * token t attends, for every head h, to the keys at absolute positions 0..positions[t] of
+ * sequence row query_seq_ids[t], found through block_tables[row, p // 16] (page) and
+ * p % 16 (row in page), using K/V head h / (heads / kv_heads).  Softmax is fp32 with scale
+ * sm_scale; output is bf16.
+ *
+ * q            : bf16 [tokens, heads, head_dim]
+ * k_pool/v_pool: bf16 [num_pages, 16, kv_heads, head_dim]
+ * block_tables : [bt_rows, bt_cols] int32 (bt_is_int64 = 0) or int64 (= 1)
+ * query_seq_ids: [tokens] int32 / int64 ; positions: [tokens] int32 / int64
+ * out          : bf16 [tokens, heads, head_dim] (may not alias q)
+ * head_dim in {64, 128}; heads % kv_heads == 0; tokens >= 1.
+ * workspace    : >= ss_attention_workspace_bytes(...) bytes, zero-filled before first use.
+ */
+SS_API int ss_ragged_paged_attention(const void* q, const int64_t q_strides[3], const void* k_pool,
+                              const int64_t k_pool_strides[4], const void* v_pool,
+                              const int64_t v_pool_strides[4], const void* block_tables,
+                              const int64_t bt_strides[2], int64_t bt_rows, int64_t bt_cols,
+                              int bt_is_int64, const void* query_seq_ids, int seq_ids_is_int64,
+                              const void* positions, int positions_is_int64, void* out,
+                              const int64_t out_strides[3], int64_t tokens, int heads,
+                              int kv_heads, int head_dim, int64_t num_pages, float sm_scale,
+                              void* workspace, size_t workspace_bytes, void* stream);
+
+/*
+ * Reads (and, if clear != 0, zeroes) the device error word at the start of `workspace`.
+ * Synchronises `stream`.  For tests and debugging, not for the hot path.
+ */
+SS_API int ss_fetch_device_errors(void* workspace, int clear, uint32_t* flags, void* stream);
+
+/*
+ * Which kernel family the last successful ss_ragged_paged_attention call on this thread
+ * used: 1 = TMA/tensor-core split-K kernel, 2 = generic strided kernel (layouts the TMA
+ * path cannot describe), 0 = none yet.  Lets tests assert the fast path really ran.
+ */
+SS_API int ss_last_attention_path(void);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* SHARDSERVE_B200_H */

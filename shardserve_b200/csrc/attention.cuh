@@ -1,0 +1,151 @@
+// Internal declarations shared by the attention / append kernels and the C-ABI layer.
+#pragma once
+
+#include <cuda.h>
+#include <cuda_bf16.h>
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#include "../../include/shardserve_b200.h"
+
+namespace ss {
+
+constexpr int kPage = SS_BLOCK_SIZE;  // tokens per KV page (reference kernel.py:8)
+
+// Arguments common to every attention kernel.  Strides are in elements.
+struct AttnArgs {
+  const __nv_bfloat16* q;
+  long long q_st, q_sh, q_sd;
+  const void* bt;
+  long long bt_sb, bt_sn;
+  int bt64;
+  const void* seq;
+  int seq64;
+  const void* pos;
+  int pos64;
+  __nv_bfloat16* out;
+  long long o_st, o_sh, o_sd;
+  const __nv_bfloat16* kp;
+  long long k_sn, k_ss, k_sh, k_sd;
+  const __nv_bfloat16* vp;
+  long long v_sn, v_ss, v_sh, v_sd;
+  long long T;  // query tokens
+  long long B;  // block-table rows
+  long long W;  // block-table columns (pages per row)
+  long long N;  // pool pages
+  int H, KVH, D, group;
+  float sm_scale;
+  float scale_log2;  // sm_scale * log2(e): softmax runs in base 2
+  unsigned* err;     // device error word (workspace byte 0)
+};
+
+// Extra state of the split-K decode kernel.
+struct DecodeArgs {
+  AttnArgs a;
+  int kvb;       // KV heads per CTA (1 or 2)
+  int nkvblk;    // KVH / kvb
+  int G;         // CTAs in the grid
+  int min_run;   // see token_in_long_run(); 0 = this launch owns every token
+  int* tickets;  // [T * nkvblk] split-K arrival counters (zero between calls)
+  float* part;   // [2 * G] partial-state slots
+};
+
+__device__ __forceinline__ long long ld_index(const void* p, int is64, long long i) {
+  return is64 ? static_cast<long long>(__ldg(static_cast<const long long*>(p) + i))
+              : static_cast<long long>(__ldg(static_cast<const int*>(p) + i));
+}
+
+struct TokInfo {
+  long long seq;  // block-table row
+  int L;          // keys attended: positions 0 .. L-1 (reference: seq_len = pos + 1, kernel.py:119)
+  int npages;     // ceil(L / 16)
+};
+
+// Decodes one query token's (sequence row, absolute position) pair.  Out-of-range values
+// are clamped to something safe and reported through the error word when `report` is set:
+//  * seq outside [0, B)          -> no keys (output zeros), SS_DEVERR_SEQ
+//  * position < 0                -> no keys (output zeros), SS_DEVERR_POS
+//  * position + 1 > 16 * W       -> keys clamped to the 16 * W the table can name, SS_DEVERR_POS
+__device__ __forceinline__ TokInfo token_info(const AttnArgs& a, long long t, bool report) {
+  TokInfo r;
+  const long long seq = ld_index(a.seq, a.seq64, t);
+  const long long pos = ld_index(a.pos, a.pos64, t);
+  unsigned e = 0;
+  long long L = pos + 1;
+  if (seq < 0 || seq >= a.B) {
+    e |= SS_DEVERR_SEQ;
+    L = 0;
+  }
+  if (pos < 0) {
+    e |= SS_DEVERR_POS;
+    L = 0;
+  } else if (L > a.W * kPage) {
+    e |= SS_DEVERR_POS;
+    L = a.W * kPage;
+  }
+  if (e && report) atomicOr(a.err, e);
+  r.seq = seq;
+  r.L = static_cast<int>(L);
+  r.npages = static_cast<int>((L + kPage - 1) / kPage);
+  return r;
+}
+
+// Chunked-prefill tokens: a token belongs to a "long run" when at least `min_run`
+// consecutive query tokens (itself included) carry its sequence id.  Such tokens are
+// processed by the tensor-core prefill kernel; every other token by the split-K decode
+// kernel.  Both kernels evaluate this same predicate, so each token has exactly one owner.
+__device__ __forceinline__ bool token_in_long_run(const AttnArgs& a, int min_run, long long t,
+                                                  long long seq) {
+  if (min_run <= 0) return false;
+  int n = 1;
+  for (long long j = t - 1; j >= 0 && n < min_run; --j) {
+    if (ld_index(a.seq, a.seq64, j) != seq) break;
+    ++n;
+  }
+  for (long long j = t + 1; j < a.T && n < min_run; ++j) {
+    if (ld_index(a.seq, a.seq64, j) != seq) break;
+    ++n;
+  }
+  return n >= min_run;
+}
+
+// ---- host-side launchers (defined next to their kernels) ------------------------------
+struct DecodeGeometry {
+  int kvb, nkvblk, G, threads;
+  size_t smem;
+  size_t tickets_bytes, part_bytes;  // workspace regions
+};
+
+// Geometry of the split-K decode kernel on `device`; false if head_dim/kv layout has no
+// decode kernel instance.
+bool decode_geometry(int device, long long tokens, int heads, int kv_heads, int head_dim,
+                     DecodeGeometry* g, const char** why);
+
+// Launches the TMA split-K decode kernel; returns a cudaError_t.
+cudaError_t launch_decode(const DecodeGeometry& g, const CUtensorMap& tmK, const CUtensorMap& tmV,
+                          const DecodeArgs& d, cudaStream_t stream);
+
+cudaError_t launch_generic_attention(const AttnArgs& a, cudaStream_t stream);
+
+struct AppendArgs {
+  const __nv_bfloat16* k;
+  long long k_st, k_sh, k_sd;
+  const __nv_bfloat16* v;
+  long long v_st, v_sh, v_sd;
+  __nv_bfloat16* kp;
+  long long kp_sn, kp_ss, kp_sh, kp_sd;
+  __nv_bfloat16* vp;
+  long long vp_sn, vp_ss, vp_sh, vp_sd;
+  const void* slots;
+  int slots64;
+  long long T, N;
+  int KVH, D;
+  unsigned* err;  // may be null
+};
+cudaError_t launch_kv_append(const AppendArgs& a, bool vectorised, cudaStream_t stream);
+
+// Workspace layout: [0, 256) header (error word at 0), then tickets, then partial slots.
+constexpr size_t kWsHeader = 256;
+inline size_t align_up(size_t x, size_t a) { return (x + a - 1) / a * a; }
+
+}  // namespace ss

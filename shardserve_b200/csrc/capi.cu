@@ -1,0 +1,275 @@
+// C ABI (include/shardserve_b200.h): argument validation, TMA descriptor encoding and
+// kernel dispatch.  Validation mirrors the reference wrapper (shardserve/kernel.py:28-49);
+// the Python layer raises KernelUnsupported before calling here, so the checks below are
+// the last line for C callers.
+#include <cuda.h>
+#include <cuda_runtime.h>
+
+#include <cmath>
+#include <cstdarg>
+#include <cstdio>
+#include <cstring>
+#include <mutex>
+#include <string>
+
+#include "attention.cuh"
+
+namespace {
+
+thread_local std::string g_message;
+thread_local int g_last_path = 0;
+
+int fail(int status, const char* fmt, ...) {
+  char buf[512];
+  va_list ap;
+  va_start(ap, fmt);
+  vsnprintf(buf, sizeof(buf), fmt, ap);
+  va_end(ap);
+  g_message = buf;
+  return status;
+}
+
+int cuda_fail(cudaError_t e, const char* what) {
+  return fail(SS_ERR_CUDA, "%s: %s", what, cudaGetErrorString(e));
+}
+
+typedef CUresult (*EncodeTiledFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*,
+                                  const cuuint64_t*, const cuuint64_t*, const cuuint32_t*,
+                                  const cuuint32_t*, CUtensorMapInterleave, CUtensorMapSwizzle,
+                                  CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+EncodeTiledFn encode_fn() {
+  static std::once_flag once;
+  static EncodeTiledFn fn = nullptr;
+  std::call_once(once, [] {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPointByVersion("cuTensorMapEncodeTiled", &p, 12000, cudaEnableDefault,
+                                         &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<EncodeTiledFn>(p);
+  });
+  return fn;
+}
+
+// 5-D view of a pool [N, 16, KVH, D] (element strides sn, ss, sh, 1) whose box is one page
+// of `kvb` heads laid out as [head][d / 64][key][d % 64] in shared memory with the 128-byte
+// swizzle: each 128-byte line holds 64 values of one key, and the 8 keys an ldmatrix reads
+// fall in 8 different swizzle phases (bank-conflict free).
+bool encode_pool_map(CUtensorMap* map, const void* base, long long N, int KVH, int D,
+                     const int64_t* st, int kvb) {
+  EncodeTiledFn fn = encode_fn();
+  if (!fn) return false;
+  cuuint64_t dims[5] = {64, 16, static_cast<cuuint64_t>(D / 64), static_cast<cuuint64_t>(KVH),
+                        static_cast<cuuint64_t>(N)};
+  cuuint64_t strides[4] = {static_cast<cuuint64_t>(st[1]) * 2, 64 * 2,
+                           static_cast<cuuint64_t>(st[2]) * 2, static_cast<cuuint64_t>(st[0]) * 2};
+  cuuint32_t box[5] = {64, 16, static_cast<cuuint32_t>(D / 64), static_cast<cuuint32_t>(kvb), 1};
+  cuuint32_t estr[5] = {1, 1, 1, 1, 1};
+  const CUresult r = fn(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 5, const_cast<void*>(base), dims,
+                        strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                        CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                        CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS;
+}
+
+// Can the TMA kernel address this pool?  Unit stride along head_dim, every other stride a
+// multiple of 8 elements (16 bytes), 16-byte aligned base, strides below 2^39 elements.
+bool pool_tma_ok(const void* base, const int64_t* st) {
+  if (st[3] != 1) return false;
+  if ((reinterpret_cast<uintptr_t>(base) & 15) != 0) return false;
+  for (int i = 0; i < 3; ++i) {
+    if (st[i] <= 0 || (st[i] % 8) != 0 || st[i] >= (1LL << 39)) return false;
+  }
+  return true;
+}
+
+bool finite_nonneg_strides(const int64_t* st, int n) {
+  for (int i = 0; i < n; ++i)
+    if (st[i] < 0) return false;
+  return true;
+}
+
+}  // namespace
+
+extern "C" {
+
+int ss_version(void) { return 100; }
+
+const char* ss_status_string(int status) {
+  switch (status) {
+    case SS_OK: return "ok";
+    case SS_ERR_INVALID: return "invalid argument";
+    case SS_ERR_UNSUPPORTED: return "unsupported";
+    case SS_ERR_CUDA: return "CUDA error";
+    case SS_ERR_WORKSPACE: return "workspace too small";
+    default: return "unknown status";
+  }
+}
+
+const char* ss_last_error_message(void) { return g_message.c_str(); }
+
+int ss_last_attention_path(void) { return g_last_path; }
+
+int ss_kv_append(const void* k, const int64_t k_strides[3], const void* v,
+                 const int64_t v_strides[3], void* k_pool, const int64_t k_pool_strides[4],
+                 void* v_pool, const int64_t v_pool_strides[4], const void* slots,
+                 int slots_is_int64, int64_t tokens, int64_t num_pages, int kv_heads,
+                 int head_dim, void* workspace, void* stream) {
+  if (tokens < 0) return fail(SS_ERR_INVALID, "tokens must be >= 0");
+  if (tokens == 0) return SS_OK;
+  if (!k || !v || !k_pool || !v_pool || !slots || !k_strides || !v_strides || !k_pool_strides ||
+      !v_pool_strides)
+    return fail(SS_ERR_INVALID, "null pointer argument");
+  if (kv_heads < 1 || head_dim < 1 || num_pages < 1)
+    return fail(SS_ERR_INVALID, "kv_heads, head_dim and num_pages must be positive");
+  if (!finite_nonneg_strides(k_strides, 3) || !finite_nonneg_strides(v_strides, 3) ||
+      !finite_nonneg_strides(k_pool_strides, 4) || !finite_nonneg_strides(v_pool_strides, 4))
+    return fail(SS_ERR_INVALID, "negative strides are not supported");
+  ss::AppendArgs a;
+  a.k = static_cast<const __nv_bfloat16*>(k);
+  a.k_st = k_strides[0]; a.k_sh = k_strides[1]; a.k_sd = k_strides[2];
+  a.v = static_cast<const __nv_bfloat16*>(v);
+  a.v_st = v_strides[0]; a.v_sh = v_strides[1]; a.v_sd = v_strides[2];
+  a.kp = static_cast<__nv_bfloat16*>(k_pool);
+  a.kp_sn = k_pool_strides[0]; a.kp_ss = k_pool_strides[1];
+  a.kp_sh = k_pool_strides[2]; a.kp_sd = k_pool_strides[3];
+  a.vp = static_cast<__nv_bfloat16*>(v_pool);
+  a.vp_sn = v_pool_strides[0]; a.vp_ss = v_pool_strides[1];
+  a.vp_sh = v_pool_strides[2]; a.vp_sd = v_pool_strides[3];
+  a.slots = slots;
+  a.slots64 = slots_is_int64 ? 1 : 0;
+  a.T = tokens;
+  a.N = num_pages;
+  a.KVH = kv_heads;
+  a.D = head_dim;
+  a.err = workspace ? static_cast<unsigned*>(workspace) : nullptr;
+  auto vec_ok = [](const void* p, const int64_t* st, int n) {
+    if ((reinterpret_cast<uintptr_t>(p) & 15) != 0 || st[n - 1] != 1) return false;
+    for (int i = 0; i < n - 1; ++i)
+      if (st[i] % 8) return false;
+    return true;
+  };
+  const bool vec = (head_dim % 8 == 0) && vec_ok(k, k_strides, 3) && vec_ok(v, v_strides, 3) &&
+                   vec_ok(k_pool, k_pool_strides, 4) && vec_ok(v_pool, v_pool_strides, 4);
+  const cudaError_t e = ss::launch_kv_append(a, vec, static_cast<cudaStream_t>(stream));
+  if (e != cudaSuccess) return cuda_fail(e, "kv_append launch");
+  return SS_OK;
+}
+
+int ss_attention_workspace_bytes(int device, int64_t tokens, int heads, int kv_heads,
+                                 int head_dim, size_t* bytes) {
+  if (!bytes) return fail(SS_ERR_INVALID, "bytes is null");
+  if (tokens < 1 || heads < 1 || kv_heads < 1 || heads % kv_heads)
+    return fail(SS_ERR_INVALID, "invalid geometry");
+  ss::DecodeGeometry g;
+  const char* why = "";
+  size_t need = ss::kWsHeader;
+  if (ss::decode_geometry(device, tokens, heads, kv_heads, head_dim, &g, &why))
+    need += g.tickets_bytes + g.part_bytes;
+  *bytes = need;
+  return SS_OK;
+}
+
+int ss_ragged_paged_attention(const void* q, const int64_t q_strides[3], const void* k_pool,
+                              const int64_t k_pool_strides[4], const void* v_pool,
+                              const int64_t v_pool_strides[4], const void* block_tables,
+                              const int64_t bt_strides[2], int64_t bt_rows, int64_t bt_cols,
+                              int bt_is_int64, const void* query_seq_ids, int seq_ids_is_int64,
+                              const void* positions, int positions_is_int64, void* out,
+                              const int64_t out_strides[3], int64_t tokens, int heads,
+                              int kv_heads, int head_dim, int64_t num_pages, float sm_scale,
+                              void* workspace, size_t workspace_bytes, void* stream) {
+  // Checks of the reference wrapper, kernel.py:28-49 (dtype/device checks live in Python).
+  if (head_dim != 64 && head_dim != 128)
+    return fail(SS_ERR_INVALID, "ragged q must be [tokens, heads, 64|128], got head_dim %d", head_dim);
+  if (tokens < 1) return fail(SS_ERR_INVALID, "ragged batch cannot be empty");
+  if (heads < 1 || kv_heads < 1 || heads % kv_heads)
+    return fail(SS_ERR_INVALID, "query heads must be divisible by KV heads");
+  if (bt_rows < 1 || bt_cols < 1) return fail(SS_ERR_INVALID, "block_tables must be non-empty");
+  if (num_pages < 1) return fail(SS_ERR_INVALID, "KV pool must hold at least one page");
+  if (!q || !k_pool || !v_pool || !block_tables || !query_seq_ids || !positions || !out ||
+      !q_strides || !k_pool_strides || !v_pool_strides || !bt_strides || !out_strides)
+    return fail(SS_ERR_INVALID, "null pointer argument");
+  if (!workspace || workspace_bytes < ss::kWsHeader)
+    return fail(SS_ERR_WORKSPACE, "a workspace of at least %zu bytes is required", ss::kWsHeader);
+  if (!std::isfinite(sm_scale)) return fail(SS_ERR_INVALID, "sm_scale must be finite");
+  if (!finite_nonneg_strides(q_strides, 3) || !finite_nonneg_strides(k_pool_strides, 4) ||
+      !finite_nonneg_strides(v_pool_strides, 4) || !finite_nonneg_strides(bt_strides, 2) ||
+      !finite_nonneg_strides(out_strides, 3))
+    return fail(SS_ERR_INVALID, "negative strides are not supported");
+
+  ss::AttnArgs a;
+  a.q = static_cast<const __nv_bfloat16*>(q);
+  a.q_st = q_strides[0]; a.q_sh = q_strides[1]; a.q_sd = q_strides[2];
+  a.bt = block_tables;
+  a.bt_sb = bt_strides[0]; a.bt_sn = bt_strides[1];
+  a.bt64 = bt_is_int64 ? 1 : 0;
+  a.seq = query_seq_ids; a.seq64 = seq_ids_is_int64 ? 1 : 0;
+  a.pos = positions; a.pos64 = positions_is_int64 ? 1 : 0;
+  a.out = static_cast<__nv_bfloat16*>(out);
+  a.o_st = out_strides[0]; a.o_sh = out_strides[1]; a.o_sd = out_strides[2];
+  a.kp = static_cast<const __nv_bfloat16*>(k_pool);
+  a.k_sn = k_pool_strides[0]; a.k_ss = k_pool_strides[1];
+  a.k_sh = k_pool_strides[2]; a.k_sd = k_pool_strides[3];
+  a.vp = static_cast<const __nv_bfloat16*>(v_pool);
+  a.v_sn = v_pool_strides[0]; a.v_ss = v_pool_strides[1];
+  a.v_sh = v_pool_strides[2]; a.v_sd = v_pool_strides[3];
+  a.T = tokens; a.B = bt_rows; a.W = bt_cols; a.N = num_pages;
+  a.H = heads; a.KVH = kv_heads; a.D = head_dim; a.group = heads / kv_heads;
+  a.sm_scale = sm_scale;
+  a.scale_log2 = sm_scale * 1.4426950408889634f;
+  a.err = static_cast<unsigned*>(workspace);
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+
+  int device = 0;
+  cudaError_t e = cudaGetDevice(&device);
+  if (e != cudaSuccess) return cuda_fail(e, "cudaGetDevice");
+
+  // ---- fast path: TMA + tensor-core split-K kernel ------------------------------------
+  ss::DecodeGeometry g;
+  const char* why = "";
+  const bool tma_layout = pool_tma_ok(k_pool, k_pool_strides) && pool_tma_ok(v_pool, v_pool_strides);
+  if (tma_layout && ss::decode_geometry(device, tokens, heads, kv_heads, head_dim, &g, &why)) {
+    const size_t need = ss::kWsHeader + g.tickets_bytes + g.part_bytes;
+    if (workspace_bytes < need)
+      return fail(SS_ERR_WORKSPACE, "workspace holds %zu bytes, %zu needed", workspace_bytes, need);
+    CUtensorMap tmK, tmV;
+    if (encode_pool_map(&tmK, k_pool, num_pages, kv_heads, head_dim, k_pool_strides, g.kvb) &&
+        encode_pool_map(&tmV, v_pool, num_pages, kv_heads, head_dim, v_pool_strides, g.kvb)) {
+      ss::DecodeArgs d;
+      d.a = a;
+      d.kvb = g.kvb;
+      d.nkvblk = g.nkvblk;
+      d.G = g.G;
+      d.min_run = 0;
+      uint8_t* ws = static_cast<uint8_t*>(workspace);
+      d.tickets = reinterpret_cast<int*>(ws + ss::kWsHeader);
+      d.part = reinterpret_cast<float*>(ws + ss::kWsHeader + g.tickets_bytes);
+      e = ss::launch_decode(g, tmK, tmV, d, s);
+      if (e != cudaSuccess) return cuda_fail(e, "decode attention launch");
+      g_last_path = 1;
+      return SS_OK;
+    }
+  }
+  // ---- generic strided path -------------------------------------------------------------
+  e = ss::launch_generic_attention(a, s);
+  if (e != cudaSuccess) return cuda_fail(e, "generic attention launch");
+  g_last_path = 2;
+  return SS_OK;
+}
+
+int ss_fetch_device_errors(void* workspace, int clear, uint32_t* flags, void* stream) {
+  if (!workspace || !flags) return fail(SS_ERR_INVALID, "null pointer argument");
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  uint32_t host = 0;
+  cudaError_t e = cudaMemcpyAsync(&host, workspace, sizeof(host), cudaMemcpyDeviceToHost, s);
+  if (e == cudaSuccess) e = cudaStreamSynchronize(s);
+  if (e == cudaSuccess && clear) e = cudaMemsetAsync(workspace, 0, sizeof(uint32_t), s);
+  if (e == cudaSuccess && clear) e = cudaStreamSynchronize(s);
+  if (e != cudaSuccess) return cuda_fail(e, "reading the device error word");
+  *flags = host;
+  return SS_OK;
+}
+
+}  // extern "C"
