@@ -144,7 +144,9 @@ struct AppendArgs {
 };
 cudaError_t launch_kv_append(const AppendArgs& a, bool vectorised, cudaStream_t stream);
 
-// Workspace layout: [0, 256) header (error word at 0), then tickets, then partial slots.
+// Workspace layout (fixed per device): [0, 256) header (error word at byte 0), then the
+// partial-state region (sized for the largest decode kernel instance), then one int ticket
+// per (token, KV block) row.  Tickets are zero between calls.
 constexpr size_t kWsHeader = 256;
 inline size_t align_up(size_t x, size_t a) { return (x + a - 1) / a * a; }
 

@@ -244,8 +244,8 @@ int ss_ragged_paged_attention(const void* q, const int64_t q_strides[3], const v
       d.G = g.G;
       d.min_run = 0;
       uint8_t* ws = static_cast<uint8_t*>(workspace);
-      d.tickets = reinterpret_cast<int*>(ws + ss::kWsHeader);
-      d.part = reinterpret_cast<float*>(ws + ss::kWsHeader + g.tickets_bytes);
+      d.part = reinterpret_cast<float*>(ws + ss::kWsHeader);
+      d.tickets = reinterpret_cast<int*>(ws + ss::kWsHeader + g.part_bytes);
       e = ss::launch_decode(g, tmK, tmV, d, s);
       if (e != cudaSuccess) return cuda_fail(e, "decode attention launch");
       g_last_path = 1;

@@ -20,6 +20,7 @@
 #include <cuda_bf16.h>
 #include <math_constants.h>
 
+#include <algorithm>
 #include <mutex>
 
 #include "attention.cuh"
@@ -624,13 +625,36 @@ int occupancy(int device, const char** why) {
   return blocks;
 }
 
+int sm_count(int device) {
+  int sms = 0;
+  if (cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, device) != cudaSuccess) return 0;
+  return sms;
+}
+
+template <int HD, int KVB>
+size_t partial_bytes_of(int device, const char** why) {
+  return static_cast<size_t>(2) * sm_count(device) * occupancy<HD, KVB>(device, why) *
+         Traits<HD, KVB>::kSlotFloats * sizeof(float);
+}
+
+// The partial-state region is sized for the largest kernel instance, so its size and the
+// offset of the ticket region behind it are the same for every call on a device: tickets
+// of one call can never alias partial states another call wrote (tickets must read zero).
+size_t partial_region_bytes(int device, const char** why) {
+  size_t m = partial_bytes_of<128, 2>(device, why);
+  m = std::max(m, partial_bytes_of<128, 1>(device, why));
+  m = std::max(m, partial_bytes_of<64, 2>(device, why));
+  m = std::max(m, partial_bytes_of<64, 1>(device, why));
+  return align_up(m, 256);
+}
+
 template <int HD, int KVB>
 bool geometry_for(int device, long long tokens, int kv_heads, DecodeGeometry* g, const char** why) {
   using Tr = Traits<HD, KVB>;
   const int per_sm = occupancy<HD, KVB>(device, why);
   if (per_sm <= 0) return false;
-  int sms = 0;
-  if (cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, device) != cudaSuccess) {
+  const int sms = sm_count(device);
+  if (sms <= 0) {
     *why = "cannot query SM count";
     return false;
   }
@@ -639,8 +663,8 @@ bool geometry_for(int device, long long tokens, int kv_heads, DecodeGeometry* g,
   g->G = sms * per_sm;
   g->threads = Tr::kThreads;
   g->smem = Tr::kSmemBytes;
+  g->part_bytes = partial_region_bytes(device, why);
   g->tickets_bytes = align_up(static_cast<size_t>(tokens) * g->nkvblk * sizeof(int), 256);
-  g->part_bytes = static_cast<size_t>(2) * g->G * Tr::kSlotFloats * sizeof(float);
   return true;
 }
 

@@ -280,3 +280,14 @@ def test_cache_object_matches_reference_layout(dev):
     flat = cache.k[1].flatten(0, 1)
     assert torch.equal(flat[t["slots"]], t["k_new"])
     assert torch.count_nonzero(cache.k[0]) == 0 and torch.count_nonzero(cache.k[2]) == 0
+
+
+def test_mixed_geometries_share_one_workspace(dev):
+    """Calls with different token counts, head layouts and head dims reuse the per-device
+    workspace in any order: the ticket region never aliases another call's partial states."""
+    order = ["chunked_mixed", "tp2_chunk_long", "config1_decode", "d64_group4",
+             "tp2_chunk_long", "mha_d64", "chunked_mixed", "long_decode", "tp2_chunk_long"]
+    for name in order:
+        inp = cases.build(name)
+        want, _ = load_golden(name)
+        check_close(run(inp, to_device(inp, dev)), want)
