@@ -131,9 +131,13 @@ def test_generic_path_for_non_unit_head_dim_stride(dev):
     inp = cases.build("tp2_decode")
     want, _ = load_golden("tp2_decode")
     t = to_device(inp, dev)
-    kp_t = t["kp"].transpose(-1, -2).contiguous().transpose(-1, -2)  # stride_d != 1
-    vp_t = t["vp"].transpose(-1, -2).contiguous().transpose(-1, -2)
-    assert kp_t.stride(-1) != 1
+    wide_k = torch.zeros((*t["kp"].shape[:-1], 2 * t["kp"].shape[-1]), dtype=torch.bfloat16,
+                         device=dev)
+    wide_v = torch.zeros_like(wide_k)
+    wide_k[..., ::2] = t["kp"]
+    wide_v[..., ::2] = t["vp"]
+    kp_t, vp_t = wide_k[..., ::2], wide_v[..., ::2]  # head_dim stride 2
+    assert kp_t.stride(-1) == 2
     out = run(inp, t, kp=kp_t, vp=vp_t)
     assert K.last_attention_path() == 2
     check_close(out, want)
