@@ -268,8 +268,10 @@ def run_ours(args, rank, world, dist):
             for i in range(S):
                 outs.append(step(batches[i % R]))
         g_attn = torch.cuda.CUDAGraph()
-        ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
-              for _ in range(S)]
+        # external=True: the records become event-record nodes of the graph, so each replay
+        # timestamps every attention launch on the stream it runs on.
+        ev = [(torch.cuda.Event(enable_timing=True, external=True),
+               torch.cuda.Event(enable_timing=True, external=True)) for _ in range(S)]
         with torch.cuda.graph(g_attn, stream=stream):
             for i in range(S):
                 b = batches[i % R]
