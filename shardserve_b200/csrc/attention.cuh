@@ -111,7 +111,7 @@ __device__ __forceinline__ bool token_in_long_run(const AttnArgs& a, int min_run
 
 // ---- host-side launchers (defined next to their kernels) ------------------------------
 struct DecodeGeometry {
-  int kvb, nkvblk, G, threads;
+  int kvb, ng, nkvblk, G, threads;
   size_t smem;
   size_t tickets_bytes, part_bytes;  // workspace regions
 };

@@ -7,16 +7,19 @@
 // B200 design (one persistent wave, balanced by KV bytes, not by tokens):
 //  * Work unit = one 16-token page of one (token, KV-head block).  A prologue scan over
 //    the query tokens gives the total U; CTA c owns units [c*chunk, (c+1)*chunk), so every
-//    CTA streams the same number of pages regardless of how ragged the contexts are.
-//  * A producer warp gathers pages through the block table and moves each page of K and V
-//    with ONE 5-D TMA box each (128-byte swizzled, no multicast) into a multi-stage ring
-//    guarded by mbarriers.  Every byte of K/V is read from HBM exactly once per call: the
-//    GROUP query heads that share a KV head all consume the same shared-memory page.
-//  * Consumer warps (2 per KV head, 8 keys each) compute S = Q.K^T and O += P.V with
-//    mma.sync bf16 tensor-core tiles (fp32 accumulate); the 16-row M dimension holds the
-//    GROUP query heads of the KV head.  Softmax max/sum use quad shuffles, base-2 exponent.
-//  * A token whose pages span several CTAs leaves fp32 partial (m, l, acc) states; the
-//    last CTA to finish it (atomic ticket, never a spin) merges them and writes bf16.
+//    CTA streams the same number of pages however ragged the contexts are.
+//  * A producer warp gathers pages through the block table and moves each page of K and of
+//    V with ONE 5-D TMA box (128-byte swizzle, no multicast) into a multi-stage ring guarded
+//    by mbarriers.  Every byte of K/V is read from HBM once per call: the GROUP query heads
+//    sharing a KV head consume the same shared-memory page.
+//  * Two consumer warps per KV head take alternate pages.  Per page a warp computes
+//    S = Q.K^T (mma.sync m16n8k16, M = query heads of the group, N = 16 keys), an fp32
+//    base-2 online softmax with quad shuffles, and O^T += V^T.P^T (M = head_dim, N = heads,
+//    K = 16 keys): P goes from the S accumulators straight into the B operand, so the P.V
+//    product wastes no padded rows and the accumulator is head_dim x 8 per warp.
+//  * A token whose pages span several CTAs leaves fp32 partial (m, l, acc) states; after a
+//    CTA has streamed all its pages it takes an atomic ticket per split row, and the last CTA
+//    of a row merges the partials and writes bf16.  No CTA ever waits for another.
 #include <cuda_bf16.h>
 #include <math_constants.h>
 
@@ -46,30 +49,34 @@ struct StageMeta {
 };
 static_assert(sizeof(StageMeta) == 32, "StageMeta layout");
 
+struct Pending {  // a split row whose ticket is taken after the CTA's last page
+  int t, b, flags, nparts, cfirst;
+};
+
 struct Ctl {
-  long long U;       // total units of this launch
-  long long chunk;   // units per CTA
-  long long u0;      // first unit of this CTA
-  long long r0;      // first row (token * nkvblk + block)
-  int off0;          // first page inside r0
-  int n_units;       // units owned by this CTA
-  int last;          // broadcast: this CTA merges the current split row
+  long long r0;  // first row (token * nkvblk + block)
+  int off0;      // first page inside r0
   int found;
+  int last;      // broadcast: this CTA merges the current split row
+  int npend;
+  Pending pend[2];
   long long red[32];
 };
 
-template <int HD, int KVB>
+template <int HD, int KVB, int NG>
 struct Traits {
-  static constexpr int kNCW = 2 * KVB;  // consumer warps: (kv head, key half)
+  static constexpr int kNCW = 2 * KVB;  // consumer warps: (KV head, page parity)
   static constexpr int kThreads = 32 * (kNCW + 1);
-  static constexpr int kSlab = kPage * KVB * HD * 2;  // one page of K (or V), KVB heads
-  static constexpr int kStages = KVB == 2 ? 3 : 6;
+  static constexpr int kMinBlocks = KVB == 2 ? 3 : 4;  // CTAs per SM the registers must allow
+  static constexpr int kSlab = kPage * KVB * HD * 2;   // one page of K (or V), KVB heads
+  static constexpr int kStages = KVB == 2 ? 3 : 5;
   static constexpr int kStageBytes = 2 * kSlab;
-  static constexpr int kRows = 16 * KVB;  // padded query rows per CTA
+  static constexpr int kRows = 16 * KVB;  // query-head rows per partial slot
   static constexpr int kSlotFloats = kRows * (HD + 2);
-  static constexpr int kMergeFloats = KVB * 16 * (HD + 2);
+  static constexpr int kAccPerThread = NG * (HD / 16) * 4;  // O^T fragment floats per lane
+  static constexpr int kMergePerHead = 32 * kAccPerThread + 32;  // acc + m[16] + l[16]
   static constexpr int kOffMerge = kStages * kStageBytes;
-  static constexpr int kOffMeta = kOffMerge + kMergeFloats * 4;
+  static constexpr int kOffMeta = kOffMerge + KVB * kMergePerHead * 4;
   static constexpr int kOffBar = kOffMeta + kStages * (int)sizeof(StageMeta);
   static constexpr int kOffCtl = kOffBar + 2 * kStages * 8;
   static constexpr int kSmemBytes = kOffCtl + (int)sizeof(Ctl) + 1024;  // +1024: base alignment
@@ -117,29 +124,32 @@ __device__ __forceinline__ long long block_excl_scan(long long v, Ctl* ctl, long
   return before + inc - v;
 }
 
-// Units (pages x KV blocks) a token contributes to this launch.
+// Units (pages x KV blocks) a token contributes to this launch; -1 marks a token of this
+// launch without keys (its output row is zeros).
 __device__ __forceinline__ long long token_units(const DecodeArgs& d, long long t, bool report,
                                                  int* npages_out) {
   const TokInfo ti = token_info(d.a, t, report);
   const bool mine = !token_in_long_run(d.a, d.min_run, t, ti.seq);
   const int np = mine ? ti.npages : 0;
   if (npages_out) *npages_out = np;
-  // A token of this launch with no keys still needs an output row (zeros): flag it with -1.
   if (mine && np == 0) return -1;
   return static_cast<long long>(np) * d.nkvblk;
 }
 
-__device__ void write_zero_token(const AttnArgs& a, long long t, int lane, int nlanes) {
+__device__ void write_zero_token(const AttnArgs& a, long long t) {
   const __nv_bfloat16 z = __float2bfloat16(0.f);
-  for (int e = lane; e < a.H * a.D; e += nlanes) {
+  for (int e = 0; e < a.H * a.D; ++e) {
     const int h = e / a.D, dd = e % a.D;
     a.out[t * a.o_st + h * a.o_sh + dd * a.o_sd] = z;
   }
 }
 
-template <int HD, int KVB>
+// A-operand fragments of Q for S = Q.K^T: rows = query heads h0 .. h0+15 of token t.
+// k-step kk holds {row r, d 16kk+2qd..+1}, {row r, d +8} and, when NG == 2, the same for
+// row r + 8.  Rows >= group are zero.
+template <int HD, int NG>
 __device__ __forceinline__ void load_q_frags(const AttnArgs& a, long long t, int h0, int group,
-                                             int lane, uint32_t (&qa)[HD / 16][4]) {
+                                             int lane, uint32_t (&qa)[HD / 16][2 * NG]) {
   const int r = lane >> 2, qd = lane & 3;
   const __nv_bfloat16* qt = a.q + t * a.q_st;
   const bool pair = (a.q_sd == 1) && ((a.q_sh & 1) == 0) && ((a.q_st & 1) == 0) &&
@@ -156,17 +166,72 @@ __device__ __forceinline__ void load_q_frags(const AttnArgs& a, long long t, int
   for (int kk = 0; kk < HD / 16; ++kk) {
     const int d0 = kk * 16 + 2 * qd;
     qa[kk][0] = ld2(r, d0);
-    qa[kk][1] = ld2(r + 8, d0);
-    qa[kk][2] = ld2(r, d0 + 8);
-    qa[kk][3] = ld2(r + 8, d0 + 8);
+    qa[kk][1] = ld2(r, d0 + 8);
+    if (NG == 2) {
+      qa[kk][2 % (2 * NG)] = ld2(r + 8, d0);
+      qa[kk][3 % (2 * NG)] = ld2(r + 8, d0 + 8);
+    }
   }
 }
 
-template <int HD, int KVB>
-__global__ void __launch_bounds__(Traits<HD, KVB>::kThreads)
+// Shared-memory address (swizzled) that lane `lane` supplies to an x4 ldmatrix reading the
+// 16 keys x 16 d block starting at d = 16 * kk of KV head g inside a page slab.  Matrices:
+// (keys 0-7, d +0..7), (keys 0-7, d +8..15), (keys 8-15, d +0..7), (keys 8-15, d +8..15).
+template <int HD>
+__device__ __forceinline__ uint32_t slab_addr(uint32_t slab, int g, int kk, int lane) {
+  const int mi = lane >> 3;
+  const int key = ((mi >> 1) << 3) + (lane & 7);
+  const int chunk16 = ((kk * 2) & 7) + (mi & 1);
+  const int row = (g * (HD / 64) + (kk >> 2)) * kPage + key;
+  return slab + row * 128 + ((chunk16 ^ (key & 7)) << 4);
+}
+
+template <int HD, int KVB, int NG>
+__device__ void cross_merge(const DecodeArgs& d, int t, int b, int flags, int nparts, int cfirst,
+                            int tid) {
+  using Tr = Traits<HD, KVB, NG>;
+  const AttnArgs& a = d.a;
+  const int group = a.group;
+  const int rows = KVB * group;
+  __nv_bfloat16* ot = a.out + static_cast<long long>(t) * a.o_st;
+  for (int e = tid; e < rows * (HD / 4); e += Tr::kNCW * 32) {
+    const int rr = e / (HD / 4);
+    const int d4 = (e % (HD / 4)) * 4;
+    const int gg = rr / group, i = rr % group;
+    const int prow = gg * 16 + i;
+    float M = -CUDART_INF_F;
+    for (int pi = 0; pi < nparts; ++pi) {
+      const int sl = 2 * (cfirst + pi) + ((pi == 0 && (flags & kFirstPartLate)) ? 1 : 0);
+      M = fmaxf(M, __ldcg(d.part + static_cast<long long>(sl) * Tr::kSlotFloats + Tr::kRows * HD + prow));
+    }
+    const float Ms = M == -CUDART_INF_F ? 0.f : M;
+    float Lsum = 0.f;
+    float4 o = make_float4(0.f, 0.f, 0.f, 0.f);
+    for (int pi = 0; pi < nparts; ++pi) {
+      const int sl = 2 * (cfirst + pi) + ((pi == 0 && (flags & kFirstPartLate)) ? 1 : 0);
+      const float* ps = d.part + static_cast<long long>(sl) * Tr::kSlotFloats;
+      const float w = ex2(__ldcg(ps + Tr::kRows * HD + prow) - Ms);
+      Lsum += __ldcg(ps + Tr::kRows * HD + Tr::kRows + prow) * w;
+      const float4 v = __ldcg(reinterpret_cast<const float4*>(ps + prow * HD + d4));
+      o.x += v.x * w;
+      o.y += v.y * w;
+      o.z += v.z * w;
+      o.w += v.w * w;
+    }
+    const float inv = Lsum > 0.f ? 1.f / Lsum : 0.f;
+    __nv_bfloat16* op = ot + static_cast<long long>((b * KVB + gg) * group + i) * a.o_sh;
+    op[d4 * a.o_sd] = __float2bfloat16(o.x * inv);
+    op[(d4 + 1) * a.o_sd] = __float2bfloat16(o.y * inv);
+    op[(d4 + 2) * a.o_sd] = __float2bfloat16(o.z * inv);
+    op[(d4 + 3) * a.o_sd] = __float2bfloat16(o.w * inv);
+  }
+}
+
+template <int HD, int KVB, int NG>
+__global__ void __launch_bounds__(Traits<HD, KVB, NG>::kThreads, Traits<HD, KVB, NG>::kMinBlocks)
     decode_attention_kernel(const __grid_constant__ CUtensorMap tmK,
                             const __grid_constant__ CUtensorMap tmV, const DecodeArgs d) {
-  using Tr = Traits<HD, KVB>;
+  using Tr = Traits<HD, KVB, NG>;
   constexpr int NT = Tr::kThreads;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
@@ -186,6 +251,8 @@ __global__ void __launch_bounds__(Traits<HD, KVB>::kThreads)
       mbar_init(bar_empty + 8 * s, Tr::kNCW);
     }
     fence_mbar_init();
+    ctl->found = 0;
+    ctl->npend = 0;
   }
   if (warp == Tr::kNCW && lane == 0) {
     prefetch_tensormap(&tmK);
@@ -204,7 +271,7 @@ __global__ void __launch_bounds__(Traits<HD, KVB>::kThreads)
       if (t < a.T) {
         const long long u = token_units(d, t, blockIdx.x == 0, nullptr);
         if (u < 0) {
-          if (t % d.G == blockIdx.x) write_zero_token(a, t, 0, 1);
+          if (t % d.G == blockIdx.x) write_zero_token(a, t);
         } else {
           s += u;
         }
@@ -216,8 +283,6 @@ __global__ void __launch_bounds__(Traits<HD, KVB>::kThreads)
   const long long u0 = static_cast<long long>(blockIdx.x) * chunk;
   if (u0 >= U) return;  // uniform across the CTA
   const int n_units = static_cast<int>(min(chunk, U - u0));
-  if (tid == 0) ctl->found = 0;
-  __syncthreads();
   long long run = 0;
   for (long long base = 0; base < a.T; base += CH) {
     long long us[ITEMS];
@@ -276,12 +341,12 @@ __global__ void __launch_bounds__(Traits<HD, KVB>::kThreads)
       }
       int np = 0;
       token_units(d, t, false, &np);
-      const TokInfo ti = token_info(a, t, false);
       if (p >= np) {
         ++r;
         p = 0;
         continue;
       }
+      const TokInfo ti = token_info(a, t, false);
       const int seg_end = min(np, p + remaining);
       const bool whole = (p == 0 && seg_end == np);
       const long long row_start = u - p;
@@ -301,7 +366,7 @@ __global__ void __launch_bounds__(Traits<HD, KVB>::kThreads)
         if (idx < seg_end) {
           const long long pid = ld_index(a.bt, a.bt64, bt_row + idx * a.bt_sn);
           if (pid < 0 || pid >= a.N) {
-            atomicOr(a.err, SS_DEVERR_PAGE);  // TMA reads zeros for the out-of-range box
+            atomicOr(a.err, SS_DEVERR_PAGE);  // the TMA box reads zeros out of range
           } else {
             page_id = static_cast<int>(pid);
           }
@@ -358,23 +423,28 @@ __global__ void __launch_bounds__(Traits<HD, KVB>::kThreads)
   }
 
   // ============================== consumer warps ======================================
-  const int g = warp >> 1;   // KV head inside the block
-  const int hk = warp & 1;   // key half: keys 8*hk .. 8*hk+7 of every page
+  const int g = warp >> 1;  // KV head inside the block
+  const int j = warp & 1;   // page parity this warp computes
   const int r = lane >> 2, qd = lane & 3;
   const int group = a.group;
-  const int key_in = hk * 8 + (lane & 7);
   const float sc = a.scale_log2;
 
-  uint32_t qa[HD / 16][4];
-  float acc[HD / 8][4];
-  float m0 = -CUDART_INF_F, m1 = -CUDART_INF_F, l0 = 0.f, l1 = 0.f;
+  uint32_t qa[HD / 16][2 * NG];
+  float acc[NG][HD / 16][4];
+  float m0 = -CUDART_INF_F, l0 = 0.f;  // head row r
+  float m1 = -CUDART_INF_F, l1 = 0.f;  // head row r + 8 (NG == 2)
 #pragma unroll
-  for (int nt = 0; nt < HD / 8; ++nt) acc[nt][0] = acc[nt][1] = acc[nt][2] = acc[nt][3] = 0.f;
+  for (int kk = 0; kk < HD / 16; ++kk)
 #pragma unroll
-  for (int kk = 0; kk < HD / 16; ++kk) qa[kk][0] = qa[kk][1] = qa[kk][2] = qa[kk][3] = 0u;
+    for (int i = 0; i < 2 * NG; ++i) qa[kk][i] = 0u;
+#pragma unroll
+  for (int n = 0; n < NG; ++n)
+#pragma unroll
+    for (int mt = 0; mt < HD / 16; ++mt) acc[n][mt][0] = acc[n][mt][1] = acc[n][mt][2] = acc[n][mt][3] = 0.f;
 
   int stage = 0;
   uint32_t phase = 0;
+  int pos = 0;  // ring position counter: page `pos` is computed by warp parity pos & 1
   while (true) {
     if (!mbar_wait(bar_full + 8 * stage, phase)) {
       atomicOr(a.err, SS_DEVERR_TIMEOUT);
@@ -384,71 +454,106 @@ __global__ void __launch_bounds__(Traits<HD, KVB>::kThreads)
     if (m.flags & kDone) break;
     const int h0 = (m.b * KVB + g) * group;
     if (m.flags & kFirst) {
-      load_q_frags<HD, KVB>(a, m.t, h0, group, lane, qa);
+      load_q_frags<HD, NG>(a, m.t, h0, group, lane, qa);
       m0 = m1 = -CUDART_INF_F;
       l0 = l1 = 0.f;
 #pragma unroll
-      for (int nt = 0; nt < HD / 8; ++nt) acc[nt][0] = acc[nt][1] = acc[nt][2] = acc[nt][3] = 0.f;
-    }
-    const uint32_t ks = sbase + stage * Tr::kStageBytes;
-    const uint32_t vs = ks + Tr::kSlab;
-
-    // ---- S = Q K^T for this warp's 8 keys (M = 16 query-head rows, N = 8 keys) -------
-    float s[4] = {0.f, 0.f, 0.f, 0.f}, s2[4] = {0.f, 0.f, 0.f, 0.f};
+      for (int n = 0; n < NG; ++n)
 #pragma unroll
-    for (int j = 0; j < HD / 32; ++j) {
-      const int row = (g * (HD / 64) + (j >> 1)) * kPage + key_in;
-      const int chunk16 = ((j & 1) << 2) + (lane >> 3);
-      const uint32_t addr = ks + row * 128 + ((chunk16 ^ (key_in & 7)) << 4);
-      uint32_t b0, b1, b2, b3;
-      ldsm_x4(addr, b0, b1, b2, b3);
-      mma_16816(s, qa[2 * j], b0, b1);
-      mma_16816(s2, qa[2 * j + 1], b2, b3);
+        for (int mt = 0; mt < HD / 16; ++mt)
+          acc[n][mt][0] = acc[n][mt][1] = acc[n][mt][2] = acc[n][mt][3] = 0.f;
     }
-    // ---- online softmax (base 2), rows r and r+8 ---------------------------------------
-    const int kpos = m.page * kPage + hk * 8 + 2 * qd;
-    float x0 = (s[0] + s2[0]) * sc, x1 = (s[1] + s2[1]) * sc;
-    float x2 = (s[2] + s2[2]) * sc, x3 = (s[3] + s2[3]) * sc;
-    if (kpos >= m.L) x0 = x2 = -CUDART_INF_F;
-    if (kpos + 1 >= m.L) x1 = x3 = -CUDART_INF_F;
-    float mx0 = fmaxf(x0, x1), mx1 = fmaxf(x2, x3);
-    mx0 = fmaxf(mx0, __shfl_xor_sync(0xffffffffu, mx0, 1));
-    mx0 = fmaxf(mx0, __shfl_xor_sync(0xffffffffu, mx0, 2));
-    mx1 = fmaxf(mx1, __shfl_xor_sync(0xffffffffu, mx1, 1));
-    mx1 = fmaxf(mx1, __shfl_xor_sync(0xffffffffu, mx1, 2));
-    const float mn0 = fmaxf(m0, mx0), mn1 = fmaxf(m1, mx1);
-    const float ms0 = mn0 == -CUDART_INF_F ? 0.f : mn0;
-    const float ms1 = mn1 == -CUDART_INF_F ? 0.f : mn1;
-    const float al0 = ex2(m0 - ms0), al1 = ex2(m1 - ms1);
-    const float p0 = ex2(x0 - ms0), p1 = ex2(x1 - ms0);
-    const float p2 = ex2(x2 - ms1), p3 = ex2(x3 - ms1);
-    l0 = l0 * al0 + p0 + p1;
-    l1 = l1 * al1 + p2 + p3;
-    m0 = mn0;
-    m1 = mn1;
+    if ((pos & 1) != j) {
+      __syncwarp();
+      if (lane == 0) mbar_arrive(bar_empty + 8 * stage);
+    } else {
+      const uint32_t ks = sbase + stage * Tr::kStageBytes;
+      const uint32_t vs = ks + Tr::kSlab;
+      // ---- S = Q K^T: 16 query-head rows x 16 keys (two n-tiles of 8 keys) -----------
+      float s0[4] = {0.f, 0.f, 0.f, 0.f}, s1[4] = {0.f, 0.f, 0.f, 0.f};
 #pragma unroll
-    for (int nt = 0; nt < HD / 8; ++nt) {
-      acc[nt][0] *= al0;
-      acc[nt][1] *= al0;
-      acc[nt][2] *= al1;
-      acc[nt][3] *= al1;
-    }
-    const uint32_t pa0 = pack_bf16(p0, p1), pa1 = pack_bf16(p2, p3);
-    // ---- O += P V (K = this warp's 8 keys, N = head_dim in tiles of 8) ---------------
+      for (int kk = 0; kk < HD / 16; ++kk) {
+        uint32_t b0, b1, b2, b3;
+        ldsm_x4(slab_addr<HD>(ks, g, kk, lane), b0, b1, b2, b3);
+        const uint32_t a_[4] = {qa[kk][0], NG == 2 ? qa[kk][2 % (2 * NG)] : 0u, qa[kk][1],
+                                NG == 2 ? qa[kk][3 % (2 * NG)] : 0u};
+        mma_16816(s0, a_, b0, b1);
+        mma_16816(s1, a_, b2, b3);
+      }
+      // ---- online softmax over this page's keys (base 2) -------------------------------
+      const int kp = m.page * kPage + 2 * qd;  // key of s0[0]; s0[1] = kp+1, s1[*] = kp+8..
+      float x[4] = {s0[0] * sc, s0[1] * sc, s1[0] * sc, s1[1] * sc};
+      if (kp >= m.L) x[0] = -CUDART_INF_F;
+      if (kp + 1 >= m.L) x[1] = -CUDART_INF_F;
+      if (kp + 8 >= m.L) x[2] = -CUDART_INF_F;
+      if (kp + 9 >= m.L) x[3] = -CUDART_INF_F;
+      float mx = fmaxf(fmaxf(x[0], x[1]), fmaxf(x[2], x[3]));
+      mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 1));
+      mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 2));
+      const float mn = fmaxf(m0, mx);
+      const float ms = mn == -CUDART_INF_F ? 0.f : mn;
+      const float al = ex2(m0 - ms);
+      float p[4];
 #pragma unroll
-    for (int j = 0; j < HD / 32; ++j) {
-      const int row = (g * (HD / 64) + (j >> 1)) * kPage + key_in;
-      const int chunk16 = ((j & 1) << 2) + (lane >> 3);
-      const uint32_t addr = vs + row * 128 + ((chunk16 ^ (key_in & 7)) << 4);
-      uint32_t v0, v1, v2, v3;
-      ldsm_x4_trans(addr, v0, v1, v2, v3);
-      mma_1688(acc[4 * j + 0], pa0, pa1, v0);
-      mma_1688(acc[4 * j + 1], pa0, pa1, v1);
-      mma_1688(acc[4 * j + 2], pa0, pa1, v2);
-      mma_1688(acc[4 * j + 3], pa0, pa1, v3);
+      for (int i = 0; i < 4; ++i) p[i] = ex2(x[i] - ms);
+      l0 = l0 * al + (p[0] + p[1]) + (p[2] + p[3]);
+      m0 = mn;
+      float al8 = 1.f;
+      float p8[4] = {0.f, 0.f, 0.f, 0.f};
+      if (NG == 2) {
+        float y[4] = {s0[2] * sc, s0[3] * sc, s1[2] * sc, s1[3] * sc};
+        if (kp >= m.L) y[0] = -CUDART_INF_F;
+        if (kp + 1 >= m.L) y[1] = -CUDART_INF_F;
+        if (kp + 8 >= m.L) y[2] = -CUDART_INF_F;
+        if (kp + 9 >= m.L) y[3] = -CUDART_INF_F;
+        float my = fmaxf(fmaxf(y[0], y[1]), fmaxf(y[2], y[3]));
+        my = fmaxf(my, __shfl_xor_sync(0xffffffffu, my, 1));
+        my = fmaxf(my, __shfl_xor_sync(0xffffffffu, my, 2));
+        const float mn8 = fmaxf(m1, my);
+        const float ms8 = mn8 == -CUDART_INF_F ? 0.f : mn8;
+        al8 = ex2(m1 - ms8);
+#pragma unroll
+        for (int i = 0; i < 4; ++i) p8[i] = ex2(y[i] - ms8);
+        l1 = l1 * al8 + (p8[0] + p8[1]) + (p8[2] + p8[3]);
+        m1 = mn8;
+      }
+      // O^T columns are query heads 2qd, 2qd+1 (+8): fetch their rescale factors.
+      if (!__all_sync(0xffffffffu, al == 1.f && al8 == 1.f)) {
+        const float c0 = __shfl_sync(0xffffffffu, al, (2 * qd) * 4);
+        const float c1 = __shfl_sync(0xffffffffu, al, (2 * qd + 1) * 4);
+#pragma unroll
+        for (int mt = 0; mt < HD / 16; ++mt) {
+          acc[0][mt][0] *= c0;
+          acc[0][mt][1] *= c1;
+          acc[0][mt][2] *= c0;
+          acc[0][mt][3] *= c1;
+        }
+        if (NG == 2) {
+          const float c8 = __shfl_sync(0xffffffffu, al8, (2 * qd) * 4);
+          const float c9 = __shfl_sync(0xffffffffu, al8, (2 * qd + 1) * 4);
+#pragma unroll
+          for (int mt = 0; mt < HD / 16; ++mt) {
+            acc[NG - 1][mt][0] *= c8;
+            acc[NG - 1][mt][1] *= c9;
+            acc[NG - 1][mt][2] *= c8;
+            acc[NG - 1][mt][3] *= c9;
+          }
+        }
+      }
+      // ---- O^T += V^T P^T: M = head_dim (16 per tile), N = 8 heads, K = 16 keys ----------
+      const uint32_t pb0 = pack_bf16(p[0], p[1]), pb1 = pack_bf16(p[2], p[3]);
+      const uint32_t pc0 = pack_bf16(p8[0], p8[1]), pc1 = pack_bf16(p8[2], p8[3]);
+#pragma unroll
+      for (int mt = 0; mt < HD / 16; ++mt) {
+        uint32_t v[4];
+        ldsm_x4_trans(slab_addr<HD>(vs, g, mt, lane), v[0], v[1], v[2], v[3]);
+        mma_16816(acc[0][mt], v, pb0, pb1);
+        if (NG == 2) mma_16816(acc[NG - 1][mt], v, pc0, pc1);
+      }
+      __syncwarp();
+      if (lane == 0) mbar_arrive(bar_empty + 8 * stage);
     }
-    __syncwarp();
-    if (lane == 0) mbar_arrive(bar_empty + 8 * stage);
+    ++pos;
     if (++stage == Tr::kStages) {
       stage = 0;
       phase ^= 1;
@@ -458,146 +563,154 @@ __global__ void __launch_bounds__(Traits<HD, KVB>::kThreads)
     // ---- end of this CTA's segment of a (token, KV block) row --------------------------
     l0 += __shfl_xor_sync(0xffffffffu, l0, 1);
     l0 += __shfl_xor_sync(0xffffffffu, l0, 2);
-    l1 += __shfl_xor_sync(0xffffffffu, l1, 1);
-    l1 += __shfl_xor_sync(0xffffffffu, l1, 2);
-    float* mg = merge + g * 16 * (HD + 2);
-    float* mg_m = mg + 16 * HD;
+    if (NG == 2) {
+      l1 += __shfl_xor_sync(0xffffffffu, l1, 1);
+      l1 += __shfl_xor_sync(0xffffffffu, l1, 2);
+    }
+    float* mg = merge + g * Tr::kMergePerHead;
+    float* mg_m = mg + 32 * Tr::kAccPerThread;
     float* mg_l = mg_m + 16;
-    if (hk == 1) {
+    if (j == 1) {  // publish the odd-page state of this head
 #pragma unroll
-      for (int nt = 0; nt < HD / 8; ++nt) {
-        *reinterpret_cast<float2*>(mg + r * HD + nt * 8 + 2 * qd) = make_float2(acc[nt][0], acc[nt][1]);
-        *reinterpret_cast<float2*>(mg + (r + 8) * HD + nt * 8 + 2 * qd) =
-            make_float2(acc[nt][2], acc[nt][3]);
-      }
+      for (int n = 0; n < NG; ++n)
+#pragma unroll
+        for (int mt = 0; mt < HD / 16; ++mt)
+#pragma unroll
+          for (int i = 0; i < 4; ++i) mg[((n * (HD / 16) + mt) * 4 + i) * 32 + lane] = acc[n][mt][i];
       if (qd == 0) {
         mg_m[r] = m0;
-        mg_m[r + 8] = m1;
         mg_l[r] = l0;
-        mg_l[r + 8] = l1;
+        if (NG == 2) {
+          mg_m[r + 8] = m1;
+          mg_l[r + 8] = l1;
+        }
       }
     }
     named_bar_sync(1, Tr::kNCW * 32);
     const bool whole = (m.flags & kWhole) != 0;
-    if (hk == 0) {
-      const float mo0 = mg_m[r], mo1 = mg_m[r + 8];
-      const float M0 = fmaxf(m0, mo0), M1 = fmaxf(m1, mo1);
-      const float Ms0 = M0 == -CUDART_INF_F ? 0.f : M0, Ms1 = M1 == -CUDART_INF_F ? 0.f : M1;
-      const float e0 = ex2(m0 - Ms0), eo0 = ex2(mo0 - Ms0);
-      const float e1 = ex2(m1 - Ms1), eo1 = ex2(mo1 - Ms1);
-      const float L0 = l0 * e0 + mg_l[r] * eo0, L1 = l1 * e1 + mg_l[r + 8] * eo1;
-#pragma unroll
-      for (int nt = 0; nt < HD / 8; ++nt) {
-        const float2 o0 = *reinterpret_cast<const float2*>(mg + r * HD + nt * 8 + 2 * qd);
-        const float2 o1 = *reinterpret_cast<const float2*>(mg + (r + 8) * HD + nt * 8 + 2 * qd);
-        acc[nt][0] = acc[nt][0] * e0 + o0.x * eo0;
-        acc[nt][1] = acc[nt][1] * e0 + o0.y * eo0;
-        acc[nt][2] = acc[nt][2] * e1 + o1.x * eo1;
-        acc[nt][3] = acc[nt][3] * e1 + o1.y * eo1;
+    if (j == 0) {
+      // Merge the two page-parity states of head row r (and r + 8).
+      const float mo = mg_m[r];
+      const float M = fmaxf(m0, mo);
+      const float Ms = M == -CUDART_INF_F ? 0.f : M;
+      const float e = ex2(m0 - Ms), eo = ex2(mo - Ms);
+      const float L = l0 * e + mg_l[r] * eo;
+      float M8 = 0.f, e8 = 1.f, eo8 = 0.f, L8 = 0.f;
+      if (NG == 2) {
+        const float mo8 = mg_m[r + 8];
+        M8 = fmaxf(m1, mo8);
+        const float Ms8 = M8 == -CUDART_INF_F ? 0.f : M8;
+        e8 = ex2(m1 - Ms8);
+        eo8 = ex2(mo8 - Ms8);
+        L8 = l1 * e8 + mg_l[r + 8] * eo8;
       }
+      // Per-column (query head) factors of the O^T fragments: heads 2qd and 2qd + 1.
+      float E[NG][2], EO[NG][2], LL[NG][2];
+#pragma unroll
+      for (int c = 0; c < 2; ++c) {
+        const int src = (2 * qd + c) * 4;
+        E[0][c] = __shfl_sync(0xffffffffu, e, src);
+        EO[0][c] = __shfl_sync(0xffffffffu, eo, src);
+        LL[0][c] = __shfl_sync(0xffffffffu, L, src);
+        if (NG == 2) {
+          E[NG - 1][c] = __shfl_sync(0xffffffffu, e8, src);
+          EO[NG - 1][c] = __shfl_sync(0xffffffffu, eo8, src);
+          LL[NG - 1][c] = __shfl_sync(0xffffffffu, L8, src);
+        }
+      }
+#pragma unroll
+      for (int n = 0; n < NG; ++n)
+#pragma unroll
+        for (int mt = 0; mt < HD / 16; ++mt)
+#pragma unroll
+          for (int i = 0; i < 4; ++i)
+            acc[n][mt][i] = acc[n][mt][i] * E[n][i & 1] +
+                            mg[((n * (HD / 16) + mt) * 4 + i) * 32 + lane] * EO[n][i & 1];
       if (whole) {
-        const float i0 = L0 > 0.f ? 1.f / L0 : 0.f, i1 = L1 > 0.f ? 1.f / L1 : 0.f;
         __nv_bfloat16* ot = a.out + static_cast<long long>(m.t) * a.o_st;
 #pragma unroll
-        for (int nt = 0; nt < HD / 8; ++nt) {
-          const int dd = nt * 8 + 2 * qd;
-          if (r < group) {
-            __nv_bfloat16* o = ot + static_cast<long long>(h0 + r) * a.o_sh;
-            o[dd * a.o_sd] = __float2bfloat16(acc[nt][0] * i0);
-            o[(dd + 1) * a.o_sd] = __float2bfloat16(acc[nt][1] * i0);
+        for (int n = 0; n < NG; ++n)
+#pragma unroll
+          for (int c = 0; c < 2; ++c) {
+            const int head = 8 * n + 2 * qd + c;
+            if (head < group) {
+              const float inv = LL[n][c] > 0.f ? 1.f / LL[n][c] : 0.f;
+              __nv_bfloat16* o = ot + static_cast<long long>(h0 + head) * a.o_sh;
+#pragma unroll
+              for (int mt = 0; mt < HD / 16; ++mt) {
+                const int dd = mt * 16 + r;
+                o[dd * a.o_sd] = __float2bfloat16(acc[n][mt][c] * inv);
+                o[(dd + 8) * a.o_sd] = __float2bfloat16(acc[n][mt][2 + c] * inv);
+              }
+            }
           }
-          if (r + 8 < group) {
-            __nv_bfloat16* o = ot + static_cast<long long>(h0 + r + 8) * a.o_sh;
-            o[dd * a.o_sd] = __float2bfloat16(acc[nt][2] * i1);
-            o[(dd + 1) * a.o_sd] = __float2bfloat16(acc[nt][3] * i1);
-          }
-        }
       } else {
         float* ps = d.part + static_cast<long long>(m.slot) * Tr::kSlotFloats;
 #pragma unroll
-        for (int nt = 0; nt < HD / 8; ++nt) {
-          const int dd = nt * 8 + 2 * qd;
-          *reinterpret_cast<float2*>(ps + (g * 16 + r) * HD + dd) = make_float2(acc[nt][0], acc[nt][1]);
-          *reinterpret_cast<float2*>(ps + (g * 16 + r + 8) * HD + dd) =
-              make_float2(acc[nt][2], acc[nt][3]);
-        }
+        for (int n = 0; n < NG; ++n)
+#pragma unroll
+          for (int c = 0; c < 2; ++c) {
+            const int head = 8 * n + 2 * qd + c;
+            float* pr = ps + (g * 16 + head) * HD;
+#pragma unroll
+            for (int mt = 0; mt < HD / 16; ++mt) {
+              pr[mt * 16 + r] = acc[n][mt][c];
+              pr[mt * 16 + r + 8] = acc[n][mt][2 + c];
+            }
+          }
         if (qd == 0) {
-          ps[Tr::kRows * HD + g * 16 + r] = M0;
-          ps[Tr::kRows * HD + g * 16 + r + 8] = M1;
-          ps[Tr::kRows * HD + Tr::kRows + g * 16 + r] = L0;
-          ps[Tr::kRows * HD + Tr::kRows + g * 16 + r + 8] = L1;
+          ps[Tr::kRows * HD + g * 16 + r] = M;
+          ps[Tr::kRows * HD + Tr::kRows + g * 16 + r] = L;
+          if (NG == 2) {
+            ps[Tr::kRows * HD + g * 16 + r + 8] = M8;
+            ps[Tr::kRows * HD + Tr::kRows + g * 16 + r + 8] = L8;
+          }
         }
-      }
-    }
-    if (!whole) {
-      // Publish the partial, take a ticket; the last of the row's CTAs merges.  No CTA
-      // ever waits for another: whoever arrives last does the work.
-      __threadfence();
-      named_bar_sync(1, Tr::kNCW * 32);
-      const long long row = static_cast<long long>(m.t) * d.nkvblk + m.b;
-      if (tid == 0) {
-        const int old = atomicAdd(d.tickets + row, 1);
-        const int last = (old == m.nparts - 1);
-        if (last) d.tickets[row] = 0;  // ready for the next call
-        ctl->last = last;
-      }
-      named_bar_sync(1, Tr::kNCW * 32);
-      if (ctl->last) {
-        __threadfence();
-        const int rows = KVB * group;
-        __nv_bfloat16* ot = a.out + static_cast<long long>(m.t) * a.o_st;
-        for (int e = tid; e < rows * (HD / 4); e += Tr::kNCW * 32) {
-          const int rr = e / (HD / 4);
-          const int d4 = (e % (HD / 4)) * 4;
-          const int gg = rr / group, i = rr % group;
-          const int prow = gg * 16 + i;
-          float M = -CUDART_INF_F;
-          for (int pi = 0; pi < m.nparts; ++pi) {
-            const int c = m.cfirst + pi;
-            const int sl = 2 * c + ((pi == 0 && (m.flags & kFirstPartLate)) ? 1 : 0);
-            M = fmaxf(M, __ldcg(d.part + static_cast<long long>(sl) * Tr::kSlotFloats + Tr::kRows * HD + prow));
-          }
-          const float Ms = M == -CUDART_INF_F ? 0.f : M;
-          float Lsum = 0.f;
-          float4 o = make_float4(0.f, 0.f, 0.f, 0.f);
-          for (int pi = 0; pi < m.nparts; ++pi) {
-            const int c = m.cfirst + pi;
-            const int sl = 2 * c + ((pi == 0 && (m.flags & kFirstPartLate)) ? 1 : 0);
-            const float* ps = d.part + static_cast<long long>(sl) * Tr::kSlotFloats;
-            const float w = ex2(__ldcg(ps + Tr::kRows * HD + prow) - Ms);
-            Lsum += __ldcg(ps + Tr::kRows * HD + Tr::kRows + prow) * w;
-            const float4 v = __ldcg(reinterpret_cast<const float4*>(ps + prow * HD + d4));
-            o.x += v.x * w;
-            o.y += v.y * w;
-            o.z += v.z * w;
-            o.w += v.w * w;
-          }
-          const float inv = Lsum > 0.f ? 1.f / Lsum : 0.f;
-          __nv_bfloat16* op = ot + static_cast<long long>((m.b * KVB + gg) * group + i) * a.o_sh;
-          op[d4 * a.o_sd] = __float2bfloat16(o.x * inv);
-          op[(d4 + 1) * a.o_sd] = __float2bfloat16(o.y * inv);
-          op[(d4 + 2) * a.o_sd] = __float2bfloat16(o.z * inv);
-          op[(d4 + 3) * a.o_sd] = __float2bfloat16(o.w * inv);
+        if (tid == 0) {
+          Pending pd;
+          pd.t = m.t;
+          pd.b = m.b;
+          pd.flags = m.flags;
+          pd.nparts = m.nparts;
+          pd.cfirst = m.cfirst;
+          ctl->pend[ctl->npend++] = pd;  // at most the CTA's first and last segments
         }
       }
     }
     named_bar_sync(1, Tr::kNCW * 32);  // merge scratch is reused by the next segment
   }
-}
 
-template <int HD, int KVB>
-struct Instance {
-  static void* fn() { return reinterpret_cast<void*>(&decode_attention_kernel<HD, KVB>); }
-};
+  // ---- split rows: publish partials, take tickets; the last CTA of a row merges -------
+  const int npend = ctl->npend;
+  if (npend == 0) return;
+  __threadfence();
+  named_bar_sync(1, Tr::kNCW * 32);
+  for (int i = 0; i < npend; ++i) {
+    const Pending pd = ctl->pend[i];
+    const long long row = static_cast<long long>(pd.t) * d.nkvblk + pd.b;
+    if (tid == 0) {
+      const int old = atomicAdd(d.tickets + row, 1);
+      const int last = (old == pd.nparts - 1);
+      if (last) d.tickets[row] = 0;  // ready for the next call
+      ctl->last = last;
+    }
+    named_bar_sync(1, Tr::kNCW * 32);
+    if (ctl->last) {
+      __threadfence();
+      cross_merge<HD, KVB, NG>(d, pd.t, pd.b, pd.flags, pd.nparts, pd.cfirst, tid);
+    }
+    named_bar_sync(1, Tr::kNCW * 32);
+  }
+}
 
 struct CachedOcc {
   int device = -1;
   int blocks = 0;
 };
 
-template <int HD, int KVB>
+template <int HD, int KVB, int NG>
 int occupancy(int device, const char** why) {
-  using Tr = Traits<HD, KVB>;
+  using Tr = Traits<HD, KVB, NG>;
   static std::mutex mu;
   static CachedOcc cache[16];
   std::lock_guard<std::mutex> lock(mu);
@@ -609,12 +722,14 @@ int occupancy(int device, const char** why) {
   int prev = 0;
   cudaGetDevice(&prev);
   if (prev != device) cudaSetDevice(device);
-  cudaError_t e = cudaFuncSetAttribute(decode_attention_kernel<HD, KVB>,
-                                       cudaFuncAttributeMaxDynamicSharedMemorySize, Tr::kSmemBytes);
+  auto fn = decode_attention_kernel<HD, KVB, NG>;
+  cudaError_t e = cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, Tr::kSmemBytes);
+  if (e == cudaSuccess)
+    e = cudaFuncSetAttribute(fn, cudaFuncAttributePreferredSharedMemoryCarveout,
+                             cudaSharedmemCarveoutMaxShared);
   int blocks = 0;
   if (e == cudaSuccess)
-    e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&blocks, decode_attention_kernel<HD, KVB>,
-                                                      Tr::kThreads, Tr::kSmemBytes);
+    e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&blocks, fn, Tr::kThreads, Tr::kSmemBytes);
   if (prev != device) cudaSetDevice(prev);
   if (e != cudaSuccess || blocks <= 0) {
     *why = "decode kernel does not fit on this device";
@@ -631,27 +746,32 @@ int sm_count(int device) {
   return sms;
 }
 
-template <int HD, int KVB>
+template <int HD, int KVB, int NG>
 size_t partial_bytes_of(int device, const char** why) {
-  return static_cast<size_t>(2) * sm_count(device) * occupancy<HD, KVB>(device, why) *
-         Traits<HD, KVB>::kSlotFloats * sizeof(float);
+  return static_cast<size_t>(2) * sm_count(device) * occupancy<HD, KVB, NG>(device, why) *
+         Traits<HD, KVB, NG>::kSlotFloats * sizeof(float);
 }
 
 // The partial-state region is sized for the largest kernel instance, so its size and the
 // offset of the ticket region behind it are the same for every call on a device: tickets
 // of one call can never alias partial states another call wrote (tickets must read zero).
 size_t partial_region_bytes(int device, const char** why) {
-  size_t m = partial_bytes_of<128, 2>(device, why);
-  m = std::max(m, partial_bytes_of<128, 1>(device, why));
-  m = std::max(m, partial_bytes_of<64, 2>(device, why));
-  m = std::max(m, partial_bytes_of<64, 1>(device, why));
+  size_t m = 0;
+  m = std::max(m, partial_bytes_of<128, 2, 1>(device, why));
+  m = std::max(m, partial_bytes_of<128, 2, 2>(device, why));
+  m = std::max(m, partial_bytes_of<128, 1, 1>(device, why));
+  m = std::max(m, partial_bytes_of<128, 1, 2>(device, why));
+  m = std::max(m, partial_bytes_of<64, 2, 1>(device, why));
+  m = std::max(m, partial_bytes_of<64, 2, 2>(device, why));
+  m = std::max(m, partial_bytes_of<64, 1, 1>(device, why));
+  m = std::max(m, partial_bytes_of<64, 1, 2>(device, why));
   return align_up(m, 256);
 }
 
-template <int HD, int KVB>
+template <int HD, int KVB, int NG>
 bool geometry_for(int device, long long tokens, int kv_heads, DecodeGeometry* g, const char** why) {
-  using Tr = Traits<HD, KVB>;
-  const int per_sm = occupancy<HD, KVB>(device, why);
+  using Tr = Traits<HD, KVB, NG>;
+  const int per_sm = occupancy<HD, KVB, NG>(device, why);
   if (per_sm <= 0) return false;
   const int sms = sm_count(device);
   if (sms <= 0) {
@@ -659,6 +779,7 @@ bool geometry_for(int device, long long tokens, int kv_heads, DecodeGeometry* g,
     return false;
   }
   g->kvb = KVB;
+  g->ng = NG;
   g->nkvblk = kv_heads / KVB;
   g->G = sms * per_sm;
   g->threads = Tr::kThreads;
@@ -666,6 +787,13 @@ bool geometry_for(int device, long long tokens, int kv_heads, DecodeGeometry* g,
   g->part_bytes = partial_region_bytes(device, why);
   g->tickets_bytes = align_up(static_cast<size_t>(tokens) * g->nkvblk * sizeof(int), 256);
   return true;
+}
+
+template <int HD, int KVB>
+bool geometry_ng(int device, long long tokens, int kv_heads, int group, DecodeGeometry* g,
+                 const char** why) {
+  return group <= 8 ? geometry_for<HD, KVB, 1>(device, tokens, kv_heads, g, why)
+                    : geometry_for<HD, KVB, 2>(device, tokens, kv_heads, g, why);
 }
 
 }  // namespace
@@ -679,12 +807,12 @@ bool decode_geometry(int device, long long tokens, int heads, int kv_heads, int 
   }
   const bool pair = (kv_heads % 2) == 0;
   if (head_dim == 128) {
-    return pair ? geometry_for<128, 2>(device, tokens, kv_heads, g, why)
-                : geometry_for<128, 1>(device, tokens, kv_heads, g, why);
+    return pair ? geometry_ng<128, 2>(device, tokens, kv_heads, group, g, why)
+                : geometry_ng<128, 1>(device, tokens, kv_heads, group, g, why);
   }
   if (head_dim == 64) {
-    return pair ? geometry_for<64, 2>(device, tokens, kv_heads, g, why)
-                : geometry_for<64, 1>(device, tokens, kv_heads, g, why);
+    return pair ? geometry_ng<64, 2>(device, tokens, kv_heads, group, g, why)
+                : geometry_ng<64, 1>(device, tokens, kv_heads, group, g, why);
   }
   *why = "head_dim must be 64 or 128";
   return false;
@@ -703,10 +831,18 @@ cudaError_t launch_decode(const DecodeGeometry& g, const CUtensorMap& tmK, const
   cfg.attrs = attr;
   cfg.numAttrs = 1;
   const int hd = d.a.D;
-  if (hd == 128 && g.kvb == 2) return cudaLaunchKernelEx(&cfg, decode_attention_kernel<128, 2>, tmK, tmV, d);
-  if (hd == 128 && g.kvb == 1) return cudaLaunchKernelEx(&cfg, decode_attention_kernel<128, 1>, tmK, tmV, d);
-  if (hd == 64 && g.kvb == 2) return cudaLaunchKernelEx(&cfg, decode_attention_kernel<64, 2>, tmK, tmV, d);
-  if (hd == 64 && g.kvb == 1) return cudaLaunchKernelEx(&cfg, decode_attention_kernel<64, 1>, tmK, tmV, d);
+#define SS_LAUNCH(HD_, KVB_, NG_)                                                              \
+  if (hd == HD_ && g.kvb == KVB_ && g.ng == NG_)                                              \
+    return cudaLaunchKernelEx(&cfg, decode_attention_kernel<HD_, KVB_, NG_>, tmK, tmV, d);
+  SS_LAUNCH(128, 2, 1)
+  SS_LAUNCH(128, 2, 2)
+  SS_LAUNCH(128, 1, 1)
+  SS_LAUNCH(128, 1, 2)
+  SS_LAUNCH(64, 2, 1)
+  SS_LAUNCH(64, 2, 2)
+  SS_LAUNCH(64, 1, 1)
+  SS_LAUNCH(64, 1, 2)
+#undef SS_LAUNCH
   return cudaErrorInvalidValue;
 }
 
