@@ -81,6 +81,7 @@ struct Traits {
   static constexpr int kOffCtl = kOffBar + 2 * kStages * 8;
   static constexpr int kSmemBytes = kOffCtl + (int)sizeof(Ctl) + 1024;  // +1024: base alignment
   static_assert(kSlab % 1024 == 0, "128B-swizzled TMA destinations must be 1024-aligned");
+  static_assert((3 + 3 * 32) * kRows * 4 <= kStages * kStageBytes, "merge scratch fits the ring");
 };
 
 // ---- block-wide reductions over all kThreads threads ---------------------------------
@@ -186,44 +187,117 @@ __device__ __forceinline__ uint32_t slab_addr(uint32_t slab, int g, int kk, int 
   return slab + row * 128 + ((chunk16 ^ (key & 7)) << 4);
 }
 
+// Merges the partial states of a split (token, KV block) row and writes its bf16 output.
+// Runs after the CTA's stream has ended, reusing the stage buffers as scratch.  Parts are
+// folded 32 at a time with an online max, so any number of parts fits; per-part weights
+// are computed once per query head, and every thread keeps several float4 loads of
+// different parts in flight (the partials sit in L2, written moments before by other SMs).
 template <int HD, int KVB, int NG>
-__device__ void cross_merge(const DecodeArgs& d, int t, int b, int flags, int nparts, int cfirst,
-                            int tid) {
+__device__ void cross_merge(const DecodeArgs& d, const Pending& pd, float* scratch, int tid) {
   using Tr = Traits<HD, KVB, NG>;
+  constexpr int NTH = Tr::kNCW * 32;
+  constexpr int R = Tr::kRows;
+  constexpr int kBatch = 32;
+  constexpr int kMaxOwn = (R * HD / 4 + NTH - 1) / NTH;
   const AttnArgs& a = d.a;
   const int group = a.group;
-  const int rows = KVB * group;
-  __nv_bfloat16* ot = a.out + static_cast<long long>(t) * a.o_st;
-  for (int e = tid; e < rows * (HD / 4); e += Tr::kNCW * 32) {
-    const int rr = e / (HD / 4);
-    const int d4 = (e % (HD / 4)) * 4;
-    const int gg = rr / group, i = rr % group;
-    const int prow = gg * 16 + i;
-    float M = -CUDART_INF_F;
-    for (int pi = 0; pi < nparts; ++pi) {
-      const int sl = 2 * (cfirst + pi) + ((pi == 0 && (flags & kFirstPartLate)) ? 1 : 0);
-      M = fmaxf(M, __ldcg(d.part + static_cast<long long>(sl) * Tr::kSlotFloats + Tr::kRows * HD + prow));
+  const int E = KVB * group * (HD / 4);  // (query head, 4 dims) elements of the output row
+  float* Mrun = scratch;                  // [R]
+  float* Lrun = Mrun + R;                 // [R]
+  float* Scl = Lrun + R;                  // [R]
+  float* Mp = Scl + R;                    // [kBatch][R]
+  float* Wp = Mp + kBatch * R;            // [kBatch][R]
+  float* Lp = Wp + kBatch * R;            // [kBatch][R]
+  for (int i = tid; i < R; i += NTH) {
+    Mrun[i] = -CUDART_INF_F;
+    Lrun[i] = 0.f;
+  }
+  float4 acc[kMaxOwn];
+#pragma unroll
+  for (int k = 0; k < kMaxOwn; ++k) acc[k] = make_float4(0.f, 0.f, 0.f, 0.f);
+  auto slot_of = [&](int pi) {
+    return 2 * (pd.cfirst + pi) + ((pi == 0 && (pd.flags & kFirstPartLate)) ? 1 : 0);
+  };
+  for (int p0 = 0; p0 < pd.nparts; p0 += kBatch) {
+    const int nb = min(kBatch, pd.nparts - p0);
+    named_bar_sync(1, NTH);
+    for (int i = tid; i < nb * R; i += NTH) {
+      const int pi = i / R, row = i % R;
+      const float* ps = d.part + static_cast<long long>(slot_of(p0 + pi)) * Tr::kSlotFloats;
+      const bool valid = (row & 15) < group;
+      Mp[pi * R + row] = valid ? __ldcg(ps + R * HD + row) : -CUDART_INF_F;
+      Lp[pi * R + row] = valid ? __ldcg(ps + R * HD + R + row) : 0.f;
     }
-    const float Ms = M == -CUDART_INF_F ? 0.f : M;
-    float Lsum = 0.f;
-    float4 o = make_float4(0.f, 0.f, 0.f, 0.f);
-    for (int pi = 0; pi < nparts; ++pi) {
-      const int sl = 2 * (cfirst + pi) + ((pi == 0 && (flags & kFirstPartLate)) ? 1 : 0);
-      const float* ps = d.part + static_cast<long long>(sl) * Tr::kSlotFloats;
-      const float w = ex2(__ldcg(ps + Tr::kRows * HD + prow) - Ms);
-      Lsum += __ldcg(ps + Tr::kRows * HD + Tr::kRows + prow) * w;
-      const float4 v = __ldcg(reinterpret_cast<const float4*>(ps + prow * HD + d4));
-      o.x += v.x * w;
-      o.y += v.y * w;
-      o.z += v.z * w;
-      o.w += v.w * w;
+    named_bar_sync(1, NTH);
+    for (int row = tid; row < R; row += NTH) {
+      float mb = Mrun[row];
+      for (int pi = 0; pi < nb; ++pi) mb = fmaxf(mb, Mp[pi * R + row]);
+      const float ms = mb == -CUDART_INF_F ? 0.f : mb;
+      const float sc = ex2(Mrun[row] - ms);
+      float l = Lrun[row] * sc;
+      for (int pi = 0; pi < nb; ++pi) {
+        const float w = ex2(Mp[pi * R + row] - ms);
+        Wp[pi * R + row] = w;
+        l += Lp[pi * R + row] * w;
+      }
+      Scl[row] = sc;
+      Mrun[row] = mb;
+      Lrun[row] = l;
     }
-    const float inv = Lsum > 0.f ? 1.f / Lsum : 0.f;
-    __nv_bfloat16* op = ot + static_cast<long long>((b * KVB + gg) * group + i) * a.o_sh;
-    op[d4 * a.o_sd] = __float2bfloat16(o.x * inv);
-    op[(d4 + 1) * a.o_sd] = __float2bfloat16(o.y * inv);
-    op[(d4 + 2) * a.o_sd] = __float2bfloat16(o.z * inv);
-    op[(d4 + 3) * a.o_sd] = __float2bfloat16(o.w * inv);
+    named_bar_sync(1, NTH);
+#pragma unroll
+    for (int k = 0; k < kMaxOwn; ++k) {
+      const int e = tid + k * NTH;
+      if (e < E) {
+        const int rr = e / (HD / 4), d4 = (e % (HD / 4)) * 4;
+        const int row = (rr / group) * 16 + rr % group;
+        const float sc = Scl[row];
+        float4 o = make_float4(acc[k].x * sc, acc[k].y * sc, acc[k].z * sc, acc[k].w * sc);
+        int pi = 0;
+        for (; pi + 4 <= nb; pi += 4) {
+          float4 v[4];
+#pragma unroll
+          for (int u = 0; u < 4; ++u)
+            v[u] = __ldcg(reinterpret_cast<const float4*>(
+                d.part + static_cast<long long>(slot_of(p0 + pi + u)) * Tr::kSlotFloats + row * HD + d4));
+#pragma unroll
+          for (int u = 0; u < 4; ++u) {
+            const float w = Wp[(pi + u) * R + row];
+            o.x += v[u].x * w;
+            o.y += v[u].y * w;
+            o.z += v[u].z * w;
+            o.w += v[u].w * w;
+          }
+        }
+        for (; pi < nb; ++pi) {
+          const float4 v = __ldcg(reinterpret_cast<const float4*>(
+              d.part + static_cast<long long>(slot_of(p0 + pi)) * Tr::kSlotFloats + row * HD + d4));
+          const float w = Wp[pi * R + row];
+          o.x += v.x * w;
+          o.y += v.y * w;
+          o.z += v.z * w;
+          o.w += v.w * w;
+        }
+        acc[k] = o;
+      }
+    }
+  }
+  named_bar_sync(1, NTH);
+  __nv_bfloat16* ot = a.out + static_cast<long long>(pd.t) * a.o_st;
+#pragma unroll
+  for (int k = 0; k < kMaxOwn; ++k) {
+    const int e = tid + k * NTH;
+    if (e < E) {
+      const int rr = e / (HD / 4), d4 = (e % (HD / 4)) * 4;
+      const int gg = rr / group, i = rr % group;
+      const float L = Lrun[gg * 16 + i];
+      const float inv = L > 0.f ? 1.f / L : 0.f;
+      __nv_bfloat16* op = ot + static_cast<long long>((pd.b * KVB + gg) * group + i) * a.o_sh;
+      op[d4 * a.o_sd] = __float2bfloat16(acc[k].x * inv);
+      op[(d4 + 1) * a.o_sd] = __float2bfloat16(acc[k].y * inv);
+      op[(d4 + 2) * a.o_sd] = __float2bfloat16(acc[k].z * inv);
+      op[(d4 + 3) * a.o_sd] = __float2bfloat16(acc[k].w * inv);
+    }
   }
 }
 
@@ -697,7 +771,8 @@ __global__ void __launch_bounds__(Traits<HD, KVB, NG>::kThreads, Traits<HD, KVB,
     named_bar_sync(1, Tr::kNCW * 32);
     if (ctl->last) {
       __threadfence();
-      cross_merge<HD, KVB, NG>(d, pd.t, pd.b, pd.flags, pd.nparts, pd.cfirst, tid);
+      // The stage ring is idle once the producer's kDone stage was consumed: scratch.
+      cross_merge<HD, KVB, NG>(d, pd, reinterpret_cast<float*>(smem), tid);
     }
     named_bar_sync(1, Tr::kNCW * 32);
   }
