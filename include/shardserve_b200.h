@@ -86,10 +86,10 @@ SS_API int ss_kv_append(const void* k, const int64_t k_strides[3], const void* v
 
 /*
  * Workspace size (bytes) that ss_ragged_paged_attention needs on `device` for this geometry.
- * The workspace must be ZERO-FILLED before its first use; every call that completes leaves
- * it ready for the next call (split-K tickets are reset by the CTA that consumes them), so
- * one buffer can be reused across calls on one stream.  Calls that run concurrently on
- * different streams need different workspaces.
+ * Byte 0..3 of the workspace is the device error word (zero it to start clean); the rest is
+ * scratch that every call rewrites before reading (split-K partial states and per-row split
+ * descriptors), so one buffer can be reused across calls on one stream without clearing.
+ * Calls that run concurrently on different streams need different workspaces.
  */
 SS_API int ss_attention_workspace_bytes(int device, int64_t tokens, int heads, int kv_heads,
                                  int head_dim, size_t* bytes);
@@ -109,7 +109,7 @@ SS_API int ss_attention_workspace_bytes(int device, int64_t tokens, int heads, i
  * query_seq_ids: [tokens] int32 / int64 ; positions: [tokens] int32 / int64
  * out          : bf16 [tokens, heads, head_dim] (may not alias q)
  * head_dim in {64, 128}; heads % kv_heads == 0; tokens >= 1.
- * workspace    : >= ss_attention_workspace_bytes(...) bytes, zero-filled before first use.
+ * workspace    : >= ss_attention_workspace_bytes(...) bytes (see above).
  */
 SS_API int ss_ragged_paged_attention(const void* q, const int64_t q_strides[3], const void* k_pool,
                               const int64_t k_pool_strides[4], const void* v_pool,

@@ -46,7 +46,8 @@ struct DecodeArgs {
   int nkvblk;    // KVH / kvb
   int G;         // CTAs in the grid
   int min_run;   // see token_in_long_run(); 0 = this launch owns every token
-  int* tickets;  // [T * nkvblk] split-K arrival counters (zero between calls)
+  int4* desc;    // [T * nkvblk] split descriptor per row: {parts (0 none, 1 whole), first
+                 // CTA, first part in the CTA's second slot, 0}; rewritten every call
   float* part;   // [2 * G] partial-state slots
 };
 
@@ -111,9 +112,9 @@ __device__ __forceinline__ bool token_in_long_run(const AttnArgs& a, int min_run
 
 // ---- host-side launchers (defined next to their kernels) ------------------------------
 struct DecodeGeometry {
-  int kvb, ng, nkvblk, G, threads;
+  int kvb, ng, nkvblk, G, threads, merge_grid;
   size_t smem;
-  size_t tickets_bytes, part_bytes;  // workspace regions
+  size_t desc_bytes, part_bytes;  // workspace regions
 };
 
 // Geometry of the split-K decode kernel on `device`; false if head_dim/kv layout has no
@@ -124,6 +125,8 @@ bool decode_geometry(int device, long long tokens, int heads, int kv_heads, int 
 // Launches the TMA split-K decode kernel; returns a cudaError_t.
 cudaError_t launch_decode(const DecodeGeometry& g, const CUtensorMap& tmK, const CUtensorMap& tmV,
                           const DecodeArgs& d, cudaStream_t stream);
+// Launches the split-K merge (programmatic dependent launch after the decode kernel).
+cudaError_t launch_merge(const DecodeGeometry& g, const DecodeArgs& d, cudaStream_t stream);
 
 cudaError_t launch_generic_attention(const AttnArgs& a, cudaStream_t stream);
 
@@ -145,8 +148,8 @@ struct AppendArgs {
 cudaError_t launch_kv_append(const AppendArgs& a, bool vectorised, cudaStream_t stream);
 
 // Workspace layout (fixed per device): [0, 256) header (error word at byte 0), then the
-// partial-state region (sized for the largest decode kernel instance), then one int ticket
-// per (token, KV block) row.  Tickets are zero between calls.
+// partial-state region (sized for the largest decode kernel instance), then one int4 split
+// descriptor per (token, KV block) row.
 constexpr size_t kWsHeader = 256;
 inline size_t align_up(size_t x, size_t a) { return (x + a - 1) / a * a; }
 

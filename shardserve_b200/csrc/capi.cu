@@ -166,7 +166,7 @@ int ss_attention_workspace_bytes(int device, int64_t tokens, int heads, int kv_h
   const char* why = "";
   size_t need = ss::kWsHeader;
   if (ss::decode_geometry(device, tokens, heads, kv_heads, head_dim, &g, &why))
-    need += g.tickets_bytes + g.part_bytes;
+    need += g.desc_bytes + g.part_bytes;
   *bytes = need;
   return SS_OK;
 }
@@ -231,7 +231,7 @@ int ss_ragged_paged_attention(const void* q, const int64_t q_strides[3], const v
   const char* why = "";
   const bool tma_layout = pool_tma_ok(k_pool, k_pool_strides) && pool_tma_ok(v_pool, v_pool_strides);
   if (tma_layout && ss::decode_geometry(device, tokens, heads, kv_heads, head_dim, &g, &why)) {
-    const size_t need = ss::kWsHeader + g.tickets_bytes + g.part_bytes;
+    const size_t need = ss::kWsHeader + g.desc_bytes + g.part_bytes;
     if (workspace_bytes < need)
       return fail(SS_ERR_WORKSPACE, "workspace holds %zu bytes, %zu needed", workspace_bytes, need);
     CUtensorMap tmK, tmV;
@@ -245,9 +245,11 @@ int ss_ragged_paged_attention(const void* q, const int64_t q_strides[3], const v
       d.min_run = 0;
       uint8_t* ws = static_cast<uint8_t*>(workspace);
       d.part = reinterpret_cast<float*>(ws + ss::kWsHeader);
-      d.tickets = reinterpret_cast<int*>(ws + ss::kWsHeader + g.part_bytes);
+      d.desc = reinterpret_cast<int4*>(ws + ss::kWsHeader + g.part_bytes);
       e = ss::launch_decode(g, tmK, tmV, d, s);
       if (e != cudaSuccess) return cuda_fail(e, "decode attention launch");
+      e = ss::launch_merge(g, d, s);
+      if (e != cudaSuccess) return cuda_fail(e, "split-K merge launch");
       g_last_path = 1;
       return SS_OK;
     }

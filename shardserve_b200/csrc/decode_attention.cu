@@ -49,17 +49,10 @@ struct StageMeta {
 };
 static_assert(sizeof(StageMeta) == 32, "StageMeta layout");
 
-struct Pending {  // a split row whose ticket is taken after the CTA's last page
-  int t, b, flags, nparts, cfirst;
-};
-
 struct Ctl {
   long long r0;  // first row (token * nkvblk + block)
   int off0;      // first page inside r0
   int found;
-  int last;      // broadcast: this CTA merges the current split row
-  int npend;
-  Pending pend[2];
   long long red[32];
 };
 
@@ -81,7 +74,6 @@ struct Traits {
   static constexpr int kOffCtl = kOffBar + 2 * kStages * 8;
   static constexpr int kSmemBytes = kOffCtl + (int)sizeof(Ctl) + 1024;  // +1024: base alignment
   static_assert(kSlab % 1024 == 0, "128B-swizzled TMA destinations must be 1024-aligned");
-  static_assert((3 + 3 * 32) * kRows * 4 <= kStages * kStageBytes, "merge scratch fits the ring");
 };
 
 // ---- block-wide reductions over all kThreads threads ---------------------------------
@@ -187,120 +179,6 @@ __device__ __forceinline__ uint32_t slab_addr(uint32_t slab, int g, int kk, int 
   return slab + row * 128 + ((chunk16 ^ (key & 7)) << 4);
 }
 
-// Merges the partial states of a split (token, KV block) row and writes its bf16 output.
-// Runs after the CTA's stream has ended, reusing the stage buffers as scratch.  Parts are
-// folded 32 at a time with an online max, so any number of parts fits; per-part weights
-// are computed once per query head, and every thread keeps several float4 loads of
-// different parts in flight (the partials sit in L2, written moments before by other SMs).
-template <int HD, int KVB, int NG>
-__device__ void cross_merge(const DecodeArgs& d, const Pending& pd, float* scratch, int tid) {
-  using Tr = Traits<HD, KVB, NG>;
-  constexpr int NTH = Tr::kNCW * 32;
-  constexpr int R = Tr::kRows;
-  constexpr int kBatch = 32;
-  constexpr int kMaxOwn = (R * HD / 4 + NTH - 1) / NTH;
-  const AttnArgs& a = d.a;
-  const int group = a.group;
-  const int E = KVB * group * (HD / 4);  // (query head, 4 dims) elements of the output row
-  float* Mrun = scratch;                  // [R]
-  float* Lrun = Mrun + R;                 // [R]
-  float* Scl = Lrun + R;                  // [R]
-  float* Mp = Scl + R;                    // [kBatch][R]
-  float* Wp = Mp + kBatch * R;            // [kBatch][R]
-  float* Lp = Wp + kBatch * R;            // [kBatch][R]
-  for (int i = tid; i < R; i += NTH) {
-    Mrun[i] = -CUDART_INF_F;
-    Lrun[i] = 0.f;
-  }
-  float4 acc[kMaxOwn];
-#pragma unroll
-  for (int k = 0; k < kMaxOwn; ++k) acc[k] = make_float4(0.f, 0.f, 0.f, 0.f);
-  auto slot_of = [&](int pi) {
-    return 2 * (pd.cfirst + pi) + ((pi == 0 && (pd.flags & kFirstPartLate)) ? 1 : 0);
-  };
-  for (int p0 = 0; p0 < pd.nparts; p0 += kBatch) {
-    const int nb = min(kBatch, pd.nparts - p0);
-    named_bar_sync(1, NTH);
-    for (int i = tid; i < nb * R; i += NTH) {
-      const int pi = i / R, row = i % R;
-      const float* ps = d.part + static_cast<long long>(slot_of(p0 + pi)) * Tr::kSlotFloats;
-      const bool valid = (row & 15) < group;
-      Mp[pi * R + row] = valid ? __ldcg(ps + R * HD + row) : -CUDART_INF_F;
-      Lp[pi * R + row] = valid ? __ldcg(ps + R * HD + R + row) : 0.f;
-    }
-    named_bar_sync(1, NTH);
-    for (int row = tid; row < R; row += NTH) {
-      float mb = Mrun[row];
-      for (int pi = 0; pi < nb; ++pi) mb = fmaxf(mb, Mp[pi * R + row]);
-      const float ms = mb == -CUDART_INF_F ? 0.f : mb;
-      const float sc = ex2(Mrun[row] - ms);
-      float l = Lrun[row] * sc;
-      for (int pi = 0; pi < nb; ++pi) {
-        const float w = ex2(Mp[pi * R + row] - ms);
-        Wp[pi * R + row] = w;
-        l += Lp[pi * R + row] * w;
-      }
-      Scl[row] = sc;
-      Mrun[row] = mb;
-      Lrun[row] = l;
-    }
-    named_bar_sync(1, NTH);
-#pragma unroll
-    for (int k = 0; k < kMaxOwn; ++k) {
-      const int e = tid + k * NTH;
-      if (e < E) {
-        const int rr = e / (HD / 4), d4 = (e % (HD / 4)) * 4;
-        const int row = (rr / group) * 16 + rr % group;
-        const float sc = Scl[row];
-        float4 o = make_float4(acc[k].x * sc, acc[k].y * sc, acc[k].z * sc, acc[k].w * sc);
-        int pi = 0;
-        for (; pi + 4 <= nb; pi += 4) {
-          float4 v[4];
-#pragma unroll
-          for (int u = 0; u < 4; ++u)
-            v[u] = __ldcg(reinterpret_cast<const float4*>(
-                d.part + static_cast<long long>(slot_of(p0 + pi + u)) * Tr::kSlotFloats + row * HD + d4));
-#pragma unroll
-          for (int u = 0; u < 4; ++u) {
-            const float w = Wp[(pi + u) * R + row];
-            o.x += v[u].x * w;
-            o.y += v[u].y * w;
-            o.z += v[u].z * w;
-            o.w += v[u].w * w;
-          }
-        }
-        for (; pi < nb; ++pi) {
-          const float4 v = __ldcg(reinterpret_cast<const float4*>(
-              d.part + static_cast<long long>(slot_of(p0 + pi)) * Tr::kSlotFloats + row * HD + d4));
-          const float w = Wp[pi * R + row];
-          o.x += v.x * w;
-          o.y += v.y * w;
-          o.z += v.z * w;
-          o.w += v.w * w;
-        }
-        acc[k] = o;
-      }
-    }
-  }
-  named_bar_sync(1, NTH);
-  __nv_bfloat16* ot = a.out + static_cast<long long>(pd.t) * a.o_st;
-#pragma unroll
-  for (int k = 0; k < kMaxOwn; ++k) {
-    const int e = tid + k * NTH;
-    if (e < E) {
-      const int rr = e / (HD / 4), d4 = (e % (HD / 4)) * 4;
-      const int gg = rr / group, i = rr % group;
-      const float L = Lrun[gg * 16 + i];
-      const float inv = L > 0.f ? 1.f / L : 0.f;
-      __nv_bfloat16* op = ot + static_cast<long long>((pd.b * KVB + gg) * group + i) * a.o_sh;
-      op[d4 * a.o_sd] = __float2bfloat16(acc[k].x * inv);
-      op[(d4 + 1) * a.o_sd] = __float2bfloat16(acc[k].y * inv);
-      op[(d4 + 2) * a.o_sd] = __float2bfloat16(acc[k].z * inv);
-      op[(d4 + 3) * a.o_sd] = __float2bfloat16(acc[k].w * inv);
-    }
-  }
-}
-
 template <int HD, int KVB, int NG>
 __global__ void __launch_bounds__(Traits<HD, KVB, NG>::kThreads, Traits<HD, KVB, NG>::kMinBlocks)
     decode_attention_kernel(const __grid_constant__ CUtensorMap tmK,
@@ -326,7 +204,6 @@ __global__ void __launch_bounds__(Traits<HD, KVB, NG>::kThreads, Traits<HD, KVB,
     }
     fence_mbar_init();
     ctl->found = 0;
-    ctl->npend = 0;
   }
   if (warp == Tr::kNCW && lane == 0) {
     prefetch_tensormap(&tmK);
@@ -334,33 +211,35 @@ __global__ void __launch_bounds__(Traits<HD, KVB, NG>::kThreads, Traits<HD, KVB,
   }
 
   // ---- prologue: total units, this CTA's range, and its first (row, page) ------------
+  // Tokens without units in this launch get their split descriptor cleared (and, for
+  // decode tokens without keys, a zero output row) by CTA t % G.
   constexpr int ITEMS = 4;
   constexpr int CH = NT * ITEMS;
+  auto note_empty = [&](long long t, long long u) {
+    if (t % d.G != blockIdx.x) return;
+    for (int b = 0; b < d.nkvblk; ++b) d.desc[t * d.nkvblk + b] = make_int4(0, 0, 0, 0);
+    if (u < 0) write_zero_token(a, t);
+  };
+  long long us[ITEMS];
+  int nps[ITEMS];
   long long U = 0;
-  for (long long base = 0; base < a.T; base += CH) {
-    long long s = 0;
+  if (a.T > CH) {  // large batches: a first pass for the total only
+    for (long long base = 0; base < a.T; base += CH) {
+      long long s = 0;
 #pragma unroll
-    for (int i = 0; i < ITEMS; ++i) {
-      const long long t = base + static_cast<long long>(tid) * ITEMS + i;
-      if (t < a.T) {
-        const long long u = token_units(d, t, blockIdx.x == 0, nullptr);
-        if (u < 0) {
-          if (t % d.G == blockIdx.x) write_zero_token(a, t);
-        } else {
-          s += u;
+      for (int i = 0; i < ITEMS; ++i) {
+        const long long t = base + static_cast<long long>(tid) * ITEMS + i;
+        if (t < a.T) {
+          const long long u = token_units(d, t, blockIdx.x == 0, nullptr);
+          if (u <= 0) note_empty(t, u);
+          s += u > 0 ? u : 0;
         }
       }
+      U += block_sum<NT>(s, ctl);
     }
-    U += block_sum<NT>(s, ctl);
   }
-  const long long chunk = max((U + d.G - 1) / d.G, static_cast<long long>(kMinChunk));
-  const long long u0 = static_cast<long long>(blockIdx.x) * chunk;
-  if (u0 >= U) return;  // uniform across the CTA
-  const int n_units = static_cast<int>(min(chunk, U - u0));
-  long long run = 0;
+  long long run = 0, chunk = 0, u0 = 0;
   for (long long base = 0; base < a.T; base += CH) {
-    long long us[ITEMS];
-    int nps[ITEMS];
     long long s = 0;
 #pragma unroll
     for (int i = 0; i < ITEMS; ++i) {
@@ -368,13 +247,18 @@ __global__ void __launch_bounds__(Traits<HD, KVB, NG>::kThreads, Traits<HD, KVB,
       us[i] = 0;
       nps[i] = 0;
       if (t < a.T) {
-        const long long u = token_units(d, t, false, &nps[i]);
-        us[i] = u < 0 ? 0 : u;
+        const long long u = token_units(d, t, a.T <= CH && blockIdx.x == 0, &nps[i]);
+        if (a.T <= CH && u <= 0) note_empty(t, u);
+        us[i] = u > 0 ? u : 0;
       }
       s += us[i];
     }
     long long total;
     long long start = run + block_excl_scan<NT>(s, ctl, total);
+    if (a.T <= CH) U = total;  // single pass: the scan also gives the total
+    chunk = max((U + d.G - 1) / d.G, static_cast<long long>(kMinChunk));
+    u0 = static_cast<long long>(blockIdx.x) * chunk;
+    if (u0 >= U) return;  // uniform across the CTA
 #pragma unroll
     for (int i = 0; i < ITEMS; ++i) {
       if (us[i] > 0 && start <= u0 && u0 < start + us[i]) {
@@ -392,6 +276,9 @@ __global__ void __launch_bounds__(Traits<HD, KVB, NG>::kThreads, Traits<HD, KVB,
   }
   __syncthreads();
   if (!ctl->found) return;  // cannot happen when u0 < U; uniform across the CTA
+  const int n_units = static_cast<int>(min(chunk, U - u0));
+  // The merge kernel that follows may be scheduled now; it waits for this grid to finish.
+  griddep_launch_dependents();
   // Everything above only read metadata the preceding kernel does not write.  From here on
   // the pool pages (appended by the preceding kernel) and the workspace are touched.
   griddep_wait();
@@ -433,6 +320,8 @@ __global__ void __launch_bounds__(Traits<HD, KVB, NG>::kThreads, Traits<HD, KVB,
         late = (row_start != cf * chunk) ? kFirstPartLate : 0;
         slot = 2 * blockIdx.x + (u == u0 ? 0 : 1);
       }
+      if (p == 0 && lane == 0)  // this CTA holds the row's first page: describe the split
+        d.desc[r] = make_int4(whole ? 1 : nparts, cfirst, late, 0);
       const long long bt_row = ti.seq * a.bt_sb;
       for (int pb = p; pb < seg_end && ok; pb += 32) {
         const int idx = pb + lane;
@@ -516,6 +405,15 @@ __global__ void __launch_bounds__(Traits<HD, KVB, NG>::kThreads, Traits<HD, KVB,
 #pragma unroll
     for (int mt = 0; mt < HD / 16; ++mt) acc[n][mt][0] = acc[n][mt][1] = acc[n][mt][2] = acc[n][mt][3] = 0.f;
 
+  // The first segment's token is known from the prologue: fetch its queries while the
+  // first pages are still in flight.
+  long long q_row = ctl->r0;
+  {
+    const long long t0 = q_row / d.nkvblk;
+    const int b0 = static_cast<int>(q_row % d.nkvblk);
+    load_q_frags<HD, NG>(a, t0, (b0 * KVB + g) * group, group, lane, qa);
+  }
+
   int stage = 0;
   uint32_t phase = 0;
   int pos = 0;  // ring position counter: page `pos` is computed by warp parity pos & 1
@@ -528,7 +426,9 @@ __global__ void __launch_bounds__(Traits<HD, KVB, NG>::kThreads, Traits<HD, KVB,
     if (m.flags & kDone) break;
     const int h0 = (m.b * KVB + g) * group;
     if (m.flags & kFirst) {
-      load_q_frags<HD, NG>(a, m.t, h0, group, lane, qa);
+      const long long row = static_cast<long long>(m.t) * d.nkvblk + m.b;
+      if (row != q_row) load_q_frags<HD, NG>(a, m.t, h0, group, lane, qa);
+      q_row = -1;
       m0 = m1 = -CUDART_INF_F;
       l0 = l1 = 0.f;
 #pragma unroll
@@ -740,41 +640,107 @@ __global__ void __launch_bounds__(Traits<HD, KVB, NG>::kThreads, Traits<HD, KVB,
             ps[Tr::kRows * HD + Tr::kRows + g * 16 + r + 8] = L8;
           }
         }
-        if (tid == 0) {
-          Pending pd;
-          pd.t = m.t;
-          pd.b = m.b;
-          pd.flags = m.flags;
-          pd.nparts = m.nparts;
-          pd.cfirst = m.cfirst;
-          ctl->pend[ctl->npend++] = pd;  // at most the CTA's first and last segments
-        }
       }
     }
     named_bar_sync(1, Tr::kNCW * 32);  // merge scratch is reused by the next segment
   }
 
-  // ---- split rows: publish partials, take tickets; the last CTA of a row merges -------
-  const int npend = ctl->npend;
-  if (npend == 0) return;
-  __threadfence();
-  named_bar_sync(1, Tr::kNCW * 32);
-  for (int i = 0; i < npend; ++i) {
-    const Pending pd = ctl->pend[i];
-    const long long row = static_cast<long long>(pd.t) * d.nkvblk + pd.b;
-    if (tid == 0) {
-      const int old = atomicAdd(d.tickets + row, 1);
-      const int last = (old == pd.nparts - 1);
-      if (last) d.tickets[row] = 0;  // ready for the next call
-      ctl->last = last;
+}
+
+// ---- split-K merge -----------------------------------------------------------------------
+// One work item = (split row, 32-dim slice of head_dim); a row split over n CTAs left n fp32
+// partial states (unnormalised O, running max m, running sum l per query head).  The CTA
+// loads every part's (m, l) into shared memory, then each thread (query head, 4 dims) folds
+// all parts with eight float4 loads in flight: a merge costs a few L2 round trips, spread
+// over many SMs.  Items are compacted per CTA first, so rows that were not split (or that
+// belong to another kernel) cost one descriptor read.
+template <int HD, int KVB>
+__global__ void __launch_bounds__(16 * KVB * 8) merge_partials_kernel(const DecodeArgs d) {
+  constexpr int R = 16 * KVB;      // query-head rows per partial slot
+  constexpr int NT = R * 8;        // (row, float4 of a 32-dim slice) per thread
+  constexpr int NSL = HD / 32;     // slices per row
+  constexpr int SF = R * (HD + 2);  // floats per partial slot
+  constexpr int kBatch = 64;
+  __shared__ float Mp[kBatch][R];
+  __shared__ float Lp[kBatch][R];
+  __shared__ long long items[NT];
+  __shared__ int nitems_s;
+  const AttnArgs& a = d.a;
+  const int tid = threadIdx.x, row = tid >> 3, f = tid & 7;
+  const int group = a.group;
+  const bool valid = (row & 15) < group;
+  griddep_wait();  // every partial and descriptor of the decode grid is visible
+  const long long nitems = a.T * d.nkvblk * NSL;
+  const long long stride = static_cast<long long>(gridDim.x) * NT;
+  for (long long base = blockIdx.x; base < nitems; base += stride) {
+    if (tid == 0) nitems_s = 0;
+    __syncthreads();
+    const long long w = base + static_cast<long long>(tid) * gridDim.x;
+    if (w < nitems && __ldcg(&d.desc[w / NSL].x) >= 2) items[atomicAdd(&nitems_s, 1)] = w;
+    __syncthreads();
+    const int n = nitems_s;
+    for (int it = 0; it < n; ++it) {
+      const long long wi = items[it];
+      const long long rr = wi / NSL;
+      const int sl = static_cast<int>(wi % NSL);
+      const int4 ds = __ldcg(&d.desc[rr]);
+      const int nparts = ds.x, cfirst = ds.y, late = ds.z;
+      auto slot_of = [&](int pi) { return 2 * (cfirst + pi) + ((pi == 0 && late) ? 1 : 0); };
+      float M = -CUDART_INF_F, L = 0.f;
+      float4 o = make_float4(0.f, 0.f, 0.f, 0.f);
+      const int dcol = sl * 32 + f * 4;
+      for (int p0 = 0; p0 < nparts; p0 += kBatch) {
+        const int nb = min(kBatch, nparts - p0);
+        __syncthreads();
+        for (int pi = f; pi < nb; pi += 8) {
+          const float* ps = d.part + static_cast<long long>(slot_of(p0 + pi)) * SF;
+          Mp[pi][row] = valid ? __ldcg(ps + R * HD + row) : -CUDART_INF_F;
+          Lp[pi][row] = valid ? __ldcg(ps + R * HD + R + row) : 0.f;
+        }
+        __syncthreads();
+        float mb = M;
+        for (int pi = 0; pi < nb; ++pi) mb = fmaxf(mb, Mp[pi][row]);
+        const float ms = mb == -CUDART_INF_F ? 0.f : mb;
+        const float scl = ex2(M - ms);
+        L *= scl;
+        o.x *= scl;
+        o.y *= scl;
+        o.z *= scl;
+        o.w *= scl;
+        M = mb;
+        if (!valid) continue;
+        for (int pi = 0; pi < nb; pi += 8) {
+          float4 v[8];
+#pragma unroll
+          for (int u = 0; u < 8; ++u)
+            if (pi + u < nb)
+              v[u] = __ldcg(reinterpret_cast<const float4*>(
+                  d.part + static_cast<long long>(slot_of(p0 + pi + u)) * SF + row * HD + dcol));
+#pragma unroll
+          for (int u = 0; u < 8; ++u)
+            if (pi + u < nb) {
+              const float wgt = ex2(Mp[pi + u][row] - ms);
+              L += Lp[pi + u][row] * wgt;
+              o.x += v[u].x * wgt;
+              o.y += v[u].y * wgt;
+              o.z += v[u].z * wgt;
+              o.w += v[u].w * wgt;
+            }
+        }
+      }
+      if (valid) {
+        const long long t = rr / d.nkvblk;
+        const int b = static_cast<int>(rr % d.nkvblk);
+        const float inv = L > 0.f ? 1.f / L : 0.f;
+        __nv_bfloat16* op = a.out + t * a.o_st +
+                            static_cast<long long>((b * KVB + (row >> 4)) * group + (row & 15)) * a.o_sh;
+        op[dcol * a.o_sd] = __float2bfloat16(o.x * inv);
+        op[(dcol + 1) * a.o_sd] = __float2bfloat16(o.y * inv);
+        op[(dcol + 2) * a.o_sd] = __float2bfloat16(o.z * inv);
+        op[(dcol + 3) * a.o_sd] = __float2bfloat16(o.w * inv);
+      }
     }
-    named_bar_sync(1, Tr::kNCW * 32);
-    if (ctl->last) {
-      __threadfence();
-      // The stage ring is idle once the producer's kDone stage was consumed: scratch.
-      cross_merge<HD, KVB, NG>(d, pd, reinterpret_cast<float*>(smem), tid);
-    }
-    named_bar_sync(1, Tr::kNCW * 32);
+    __syncthreads();
   }
 }
 
@@ -828,8 +794,7 @@ size_t partial_bytes_of(int device, const char** why) {
 }
 
 // The partial-state region is sized for the largest kernel instance, so its size and the
-// offset of the ticket region behind it are the same for every call on a device: tickets
-// of one call can never alias partial states another call wrote (tickets must read zero).
+// offset of the descriptor region behind it are the same for every call on a device.
 size_t partial_region_bytes(int device, const char** why) {
   size_t m = 0;
   m = std::max(m, partial_bytes_of<128, 2, 1>(device, why));
@@ -860,7 +825,8 @@ bool geometry_for(int device, long long tokens, int kv_heads, DecodeGeometry* g,
   g->threads = Tr::kThreads;
   g->smem = Tr::kSmemBytes;
   g->part_bytes = partial_region_bytes(device, why);
-  g->tickets_bytes = align_up(static_cast<size_t>(tokens) * g->nkvblk * sizeof(int), 256);
+  g->desc_bytes = align_up(static_cast<size_t>(tokens) * g->nkvblk * sizeof(int4), 256);
+  g->merge_grid = sms * 8;
   return true;
 }
 
@@ -918,6 +884,24 @@ cudaError_t launch_decode(const DecodeGeometry& g, const CUtensorMap& tmK, const
   SS_LAUNCH(64, 1, 1)
   SS_LAUNCH(64, 1, 2)
 #undef SS_LAUNCH
+  return cudaErrorInvalidValue;
+}
+
+cudaError_t launch_merge(const DecodeGeometry& g, const DecodeArgs& d, cudaStream_t stream) {
+  const long long items = d.a.T * d.nkvblk * (d.a.D / 32);
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(static_cast<unsigned>(std::min<long long>(items, g.merge_grid)));
+  cfg.blockDim = dim3(16 * g.kvb * 8);
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  if (d.a.D == 128 && g.kvb == 2) return cudaLaunchKernelEx(&cfg, merge_partials_kernel<128, 2>, d);
+  if (d.a.D == 128 && g.kvb == 1) return cudaLaunchKernelEx(&cfg, merge_partials_kernel<128, 1>, d);
+  if (d.a.D == 64 && g.kvb == 2) return cudaLaunchKernelEx(&cfg, merge_partials_kernel<64, 2>, d);
+  if (d.a.D == 64 && g.kvb == 1) return cudaLaunchKernelEx(&cfg, merge_partials_kernel<64, 1>, d);
   return cudaErrorInvalidValue;
 }
 

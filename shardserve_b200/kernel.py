@@ -35,11 +35,11 @@ _workspaces: dict[int, Any] = {}
 
 
 def _workspace(device, tokens: int, heads: int, kv_heads: int, head_dim: int):
-    """Per-device zero-initialised workspace (error word, split-K tickets, partial states).
+    """Per-device workspace (error word, split-K partial states, split descriptors).
 
-    Every completed call leaves the ticket region zeroed again, so the buffer is reused
-    without clearing.  One buffer per device: calls on one device must not overlap in time
-    on different streams (the reference issues them from one thread on one stream).
+    Every call rewrites the scratch it reads, so the buffer is reused without clearing.
+    One buffer per device: calls on one device must not overlap in time on different
+    streams (the reference issues them from one thread on one stream).
     """
     import torch
 
