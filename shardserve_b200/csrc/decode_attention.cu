@@ -279,10 +279,6 @@ __global__ void __launch_bounds__(Traits<HD, KVB, NG>::kThreads, Traits<HD, KVB,
   const int n_units = static_cast<int>(min(chunk, U - u0));
   // The merge kernel that follows may be scheduled now; it waits for this grid to finish.
   griddep_launch_dependents();
-  // Everything above only read metadata the preceding kernel does not write.  From here on
-  // the pool pages (appended by the preceding kernel) and the workspace are touched.
-  griddep_wait();
-
   if (warp == Tr::kNCW) {
     // ============================ producer warp ====================================
     const uint64_t policy = l2_policy_evict_first();
@@ -293,6 +289,22 @@ __global__ void __launch_bounds__(Traits<HD, KVB, NG>::kThreads, Traits<HD, KVB,
     int stage = 0;
     uint32_t phase = 0;
     bool ok = true;
+    // Block-table entries of the first 32 pages do not depend on the preceding kernel:
+    // fetch them before waiting for it.
+    int pf_page = -1;
+    {
+      const long long t = r / d.nkvblk;
+      const TokInfo ti = token_info(a, t, false);
+      const int idx = p + lane;
+      if (idx < min(ti.npages, p + remaining)) {
+        const long long pid = ld_index(a.bt, a.bt64, ti.seq * a.bt_sb + idx * a.bt_sn);
+        pf_page = (pid < 0 || pid >= a.N) ? -2 : static_cast<int>(pid);
+      }
+    }
+    bool use_pf = true;
+    // From here on the pool pages (appended by the preceding kernel) and the workspace
+    // are touched.
+    griddep_wait();
     while (remaining > 0 && ok) {
       const long long t = r / d.nkvblk;
       const int b = static_cast<int>(r % d.nkvblk);
@@ -327,13 +339,19 @@ __global__ void __launch_bounds__(Traits<HD, KVB, NG>::kThreads, Traits<HD, KVB,
         const int idx = pb + lane;
         int page_id = -1;
         if (idx < seg_end) {
-          const long long pid = ld_index(a.bt, a.bt64, bt_row + idx * a.bt_sn);
+          long long pid;
+          if (use_pf) {
+            pid = pf_page == -2 ? -1 : pf_page;
+          } else {
+            pid = ld_index(a.bt, a.bt64, bt_row + idx * a.bt_sn);
+          }
           if (pid < 0 || pid >= a.N) {
             atomicOr(a.err, SS_DEVERR_PAGE);  // the TMA box reads zeros out of range
           } else {
             page_id = static_cast<int>(pid);
           }
         }
+        use_pf = false;
         const int cnt = min(32, seg_end - pb);
         for (int k = 0; k < cnt; ++k) {
           const int pg = __shfl_sync(0xffffffffu, page_id, k);
@@ -386,6 +404,7 @@ __global__ void __launch_bounds__(Traits<HD, KVB, NG>::kThreads, Traits<HD, KVB,
   }
 
   // ============================== consumer warps ======================================
+  griddep_wait();
   const int g = warp >> 1;  // KV head inside the block
   const int j = warp & 1;   // page parity this warp computes
   const int r = lane >> 2, qd = lane & 3;
@@ -660,10 +679,12 @@ __global__ void __launch_bounds__(16 * KVB * 8) merge_partials_kernel(const Deco
   constexpr int NT = R * 8;        // (row, float4 of a 32-dim slice) per thread
   constexpr int NSL = HD / 32;     // slices per row
   constexpr int SF = R * (HD + 2);  // floats per partial slot
-  constexpr int kBatch = 64;
+  constexpr int kDirect = 16;      // parts folded from registers in one round trip
+  constexpr int kBatch = 64;       // parts per shared-memory batch beyond that
   __shared__ float Mp[kBatch][R];
   __shared__ float Lp[kBatch][R];
   __shared__ long long items[NT];
+  __shared__ int4 descs[NT];
   __shared__ int nitems_s;
   const AttnArgs& a = d.a;
   const int tid = threadIdx.x, row = tid >> 3, f = tid & 7;
@@ -676,56 +697,96 @@ __global__ void __launch_bounds__(16 * KVB * 8) merge_partials_kernel(const Deco
     if (tid == 0) nitems_s = 0;
     __syncthreads();
     const long long w = base + static_cast<long long>(tid) * gridDim.x;
-    if (w < nitems && __ldcg(&d.desc[w / NSL].x) >= 2) items[atomicAdd(&nitems_s, 1)] = w;
+    if (w < nitems) {
+      const int4 ds = __ldcg(&d.desc[w / NSL]);
+      if (ds.x >= 2) {
+        const int k = atomicAdd(&nitems_s, 1);
+        items[k] = w;
+        descs[k] = ds;
+      }
+    }
     __syncthreads();
     const int n = nitems_s;
     for (int it = 0; it < n; ++it) {
       const long long wi = items[it];
       const long long rr = wi / NSL;
       const int sl = static_cast<int>(wi % NSL);
-      const int4 ds = __ldcg(&d.desc[rr]);
+      const int4 ds = descs[it];
       const int nparts = ds.x, cfirst = ds.y, late = ds.z;
-      auto slot_of = [&](int pi) { return 2 * (cfirst + pi) + ((pi == 0 && late) ? 1 : 0); };
-      float M = -CUDART_INF_F, L = 0.f;
-      float4 o = make_float4(0.f, 0.f, 0.f, 0.f);
+      auto slot_ptr = [&](int pi) {
+        return d.part + static_cast<long long>(2 * (cfirst + pi) + ((pi == 0 && late) ? 1 : 0)) * SF;
+      };
       const int dcol = sl * 32 + f * 4;
-      for (int p0 = 0; p0 < nparts; p0 += kBatch) {
-        const int nb = min(kBatch, nparts - p0);
-        __syncthreads();
-        for (int pi = f; pi < nb; pi += 8) {
-          const float* ps = d.part + static_cast<long long>(slot_of(p0 + pi)) * SF;
-          Mp[pi][row] = valid ? __ldcg(ps + R * HD + row) : -CUDART_INF_F;
-          Lp[pi][row] = valid ? __ldcg(ps + R * HD + R + row) : 0.f;
+      float L = 0.f;
+      float4 o = make_float4(0.f, 0.f, 0.f, 0.f);
+      if (nparts <= kDirect) {
+        // One round trip: every part's (m, l, 4 values) of this thread's head row.
+        float mv[kDirect], lv[kDirect];
+        float4 vv[kDirect];
+#pragma unroll
+        for (int u = 0; u < kDirect; ++u) {
+          mv[u] = -CUDART_INF_F;
+          lv[u] = 0.f;
+          vv[u] = make_float4(0.f, 0.f, 0.f, 0.f);
+          if (u < nparts && valid) {
+            const float* ps = slot_ptr(u);
+            mv[u] = __ldcg(ps + R * HD + row);
+            lv[u] = __ldcg(ps + R * HD + R + row);
+            vv[u] = __ldcg(reinterpret_cast<const float4*>(ps + row * HD + dcol));
+          }
         }
-        __syncthreads();
-        float mb = M;
-        for (int pi = 0; pi < nb; ++pi) mb = fmaxf(mb, Mp[pi][row]);
-        const float ms = mb == -CUDART_INF_F ? 0.f : mb;
-        const float scl = ex2(M - ms);
-        L *= scl;
-        o.x *= scl;
-        o.y *= scl;
-        o.z *= scl;
-        o.w *= scl;
-        M = mb;
-        if (!valid) continue;
-        for (int pi = 0; pi < nb; pi += 8) {
-          float4 v[8];
+        float M = -CUDART_INF_F;
 #pragma unroll
-          for (int u = 0; u < 8; ++u)
-            if (pi + u < nb)
-              v[u] = __ldcg(reinterpret_cast<const float4*>(
-                  d.part + static_cast<long long>(slot_of(p0 + pi + u)) * SF + row * HD + dcol));
+        for (int u = 0; u < kDirect; ++u) M = fmaxf(M, mv[u]);
+        const float ms = M == -CUDART_INF_F ? 0.f : M;
 #pragma unroll
-          for (int u = 0; u < 8; ++u)
-            if (pi + u < nb) {
-              const float wgt = ex2(Mp[pi + u][row] - ms);
-              L += Lp[pi + u][row] * wgt;
-              o.x += v[u].x * wgt;
-              o.y += v[u].y * wgt;
-              o.z += v[u].z * wgt;
-              o.w += v[u].w * wgt;
-            }
+        for (int u = 0; u < kDirect; ++u) {
+          const float wgt = ex2(mv[u] - ms);
+          L += lv[u] * wgt;
+          o.x += vv[u].x * wgt;
+          o.y += vv[u].y * wgt;
+          o.z += vv[u].z * wgt;
+          o.w += vv[u].w * wgt;
+        }
+      } else {
+        float M = -CUDART_INF_F;
+        for (int p0 = 0; p0 < nparts; p0 += kBatch) {
+          const int nb = min(kBatch, nparts - p0);
+          __syncthreads();
+          for (int pi = f; pi < nb; pi += 8) {
+            const float* ps = slot_ptr(p0 + pi);
+            Mp[pi][row] = valid ? __ldcg(ps + R * HD + row) : -CUDART_INF_F;
+            Lp[pi][row] = valid ? __ldcg(ps + R * HD + R + row) : 0.f;
+          }
+          __syncthreads();
+          float mb = M;
+          for (int pi = 0; pi < nb; ++pi) mb = fmaxf(mb, Mp[pi][row]);
+          const float ms = mb == -CUDART_INF_F ? 0.f : mb;
+          const float scl = ex2(M - ms);
+          L *= scl;
+          o.x *= scl;
+          o.y *= scl;
+          o.z *= scl;
+          o.w *= scl;
+          M = mb;
+          if (!valid) continue;
+          for (int pi = 0; pi < nb; pi += 8) {
+            float4 v[8];
+#pragma unroll
+            for (int u = 0; u < 8; ++u)
+              if (pi + u < nb)
+                v[u] = __ldcg(reinterpret_cast<const float4*>(slot_ptr(p0 + pi + u) + row * HD + dcol));
+#pragma unroll
+            for (int u = 0; u < 8; ++u)
+              if (pi + u < nb) {
+                const float wgt = ex2(Mp[pi + u][row] - ms);
+                L += Lp[pi + u][row] * wgt;
+                o.x += v[u].x * wgt;
+                o.y += v[u].y * wgt;
+                o.z += v[u].z * wgt;
+                o.w += v[u].w * wgt;
+              }
+          }
         }
       }
       if (valid) {
