@@ -122,6 +122,32 @@ SS_API int ss_ragged_paged_attention(const void* q, const int64_t q_strides[3], 
                               void* workspace, size_t workspace_bytes, void* stream);
 
 /*
+ * ss_ragged_paged_attention without a workspace argument: allocation-free.  No counterpart
+ * in the reference; it exists for callers that cannot allocate device memory around the
+ * call, such as code being recorded into a CUDA graph (cudaMalloc is illegal during stream
+ * capture), serving loops that plan all device memory ahead and must never stall on an
+ * allocator, and plain C / FFI hosts without a caching allocator to keep a workspace alive.
+ *
+ * The split-K scratch is a fixed 16 MiB array of this library's own device memory
+ * (file-scope __device__ storage, present on every GPU that loads the library until the
+ * process exits).  Calls whose scratch need (ss_attention_workspace_bytes) exceeds it are
+ * rejected with SS_ERR_WORKSPACE and a message; use ss_ragged_paged_attention instead.
+ * The first call on a device looks up the array's device address (cudaGetSymbolAddress) and
+ * the kernels' launch attributes; make that first call before any stream capture.  All
+ * calls on a device share the one array and each call overwrites it (its error word is
+ * cleared at the start of every call), so calls that can overlap on the GPU (different
+ * streams, or concurrent graph replays) race and must be serialised by the caller.
+ * Arguments and results are those of ss_ragged_paged_attention.
+ */
+SS_API int ss_ragged_paged_attention_noalloc(
+    const void* q, const int64_t q_strides[3], const void* k_pool, const int64_t k_pool_strides[4],
+    const void* v_pool, const int64_t v_pool_strides[4], const void* block_tables,
+    const int64_t bt_strides[2], int64_t bt_rows, int64_t bt_cols, int bt_is_int64,
+    const void* query_seq_ids, int seq_ids_is_int64, const void* positions,
+    int positions_is_int64, void* out, const int64_t out_strides[3], int64_t tokens, int heads,
+    int kv_heads, int head_dim, int64_t num_pages, float sm_scale, void* stream);
+
+/*
  * Reads (and, if clear != 0, zeroes) the device error word at the start of `workspace`.
  * Synchronises `stream`.  For tests and debugging, not for the hot path.
  */

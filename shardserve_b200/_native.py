@@ -46,6 +46,10 @@ SIGNATURES = {
         ctypes.c_int, _vp, ctypes.c_int, _vp, ctypes.c_int, _vp, _i64p, ctypes.c_int64,
         ctypes.c_int, ctypes.c_int, ctypes.c_int, ctypes.c_int64, ctypes.c_float, _vp,
         ctypes.c_size_t, _vp]),
+    "ss_ragged_paged_attention_noalloc": (ctypes.c_int, [
+        _vp, _i64p, _vp, _i64p, _vp, _i64p, _vp, _i64p, ctypes.c_int64, ctypes.c_int64,
+        ctypes.c_int, _vp, ctypes.c_int, _vp, ctypes.c_int, _vp, _i64p, ctypes.c_int64,
+        ctypes.c_int, ctypes.c_int, ctypes.c_int, ctypes.c_int64, ctypes.c_float, _vp]),
     "ss_fetch_device_errors": (ctypes.c_int, [
         _vp, ctypes.c_int, ctypes.POINTER(ctypes.c_uint32), _vp]),
     "ss_last_attention_path": (ctypes.c_int, []),

@@ -147,6 +147,9 @@ struct AppendArgs {
 };
 cudaError_t launch_kv_append(const AppendArgs& a, bool vectorised, cudaStream_t stream);
 
+// Sets the text ss_last_error_message() returns on this thread (printf-style).
+void set_error_message(const char* fmt, ...);
+
 // Workspace layout (fixed per device): [0, 256) header (error word at byte 0), then the
 // partial-state region (sized for the largest decode kernel instance), then one int4 split
 // descriptor per (token, KV block) row.

@@ -92,6 +92,17 @@ bool finite_nonneg_strides(const int64_t* st, int n) {
 
 }  // namespace
 
+namespace ss {
+void set_error_message(const char* fmt, ...) {
+  char buf[512];
+  va_list ap;
+  va_start(ap, fmt);
+  vsnprintf(buf, sizeof(buf), fmt, ap);
+  va_end(ap);
+  g_message = buf;
+}
+}  // namespace ss
+
 extern "C" {
 
 int ss_version(void) { return 100; }
