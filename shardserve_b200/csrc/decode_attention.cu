@@ -46,8 +46,10 @@ struct StageMeta {
   int slot;    // partial slot written by this CTA (split rows)
   int nparts;  // CTAs sharing this row (split rows)
   int cfirst;  // first CTA of this row (split rows)
+  int next_row;  // row of this CTA's next segment (-1: none); lets consumers prefetch its q
+  int pad[3];
 };
-static_assert(sizeof(StageMeta) == 32, "StageMeta layout");
+static_assert(sizeof(StageMeta) == 48, "StageMeta layout");
 
 struct Ctl {
   long long r0;  // first row (token * nkvblk + block)
@@ -68,8 +70,11 @@ struct Traits {
   static constexpr int kSlotFloats = kRows * (HD + 2);
   static constexpr int kAccPerThread = NG * (HD / 16) * 4;  // O^T fragment floats per lane
   static constexpr int kMergePerHead = 32 * kAccPerThread + 32;  // acc + m[16] + l[16]
+  static constexpr int kQRows = 8 * NG;  // query-head rows a consumer warp prefetches
+  static constexpr int kQBufBytes = kQRows * HD * 2;  // one row block of q, bf16
   static constexpr int kOffMerge = kStages * kStageBytes;
-  static constexpr int kOffMeta = kOffMerge + KVB * kMergePerHead * 4;
+  static constexpr int kOffQ = kOffMerge + KVB * kMergePerHead * 4;  // [warp][2][kQBufBytes]
+  static constexpr int kOffMeta = kOffQ + kNCW * 2 * kQBufBytes;
   static constexpr int kOffBar = kOffMeta + kStages * (int)sizeof(StageMeta);
   static constexpr int kOffCtl = kOffBar + 2 * kStages * 8;
   static constexpr int kSmemBytes = kOffCtl + (int)sizeof(Ctl) + 1024;  // +1024: base alignment
@@ -334,6 +339,17 @@ __global__ void __launch_bounds__(Traits<HD, KVB, NG>::kThreads, Traits<HD, KVB,
       }
       if (p == 0 && lane == 0)  // this CTA holds the row's first page: describe the split
         d.desc[r] = make_int4(whole ? 1 : nparts, cfirst, late, 0);
+      int next_row = -1;  // the next row with pages inside this CTA's range, if any
+      if (remaining > seg_end - p) {
+        for (long long r2 = r + 1; r2 < a.T * d.nkvblk; ++r2) {
+          int np2 = 0;
+          token_units(d, r2 / d.nkvblk, false, &np2);
+          if (np2 > 0) {
+            next_row = static_cast<int>(r2);
+            break;
+          }
+        }
+      }
       const long long bt_row = ti.seq * a.bt_sb;
       for (int pb = p; pb < seg_end && ok; pb += 32) {
         const int idx = pb + lane;
@@ -369,6 +385,7 @@ __global__ void __launch_bounds__(Traits<HD, KVB, NG>::kThreads, Traits<HD, KVB,
               m.slot = slot;
               m.nparts = nparts;
               m.cfirst = cfirst;
+              m.next_row = next_row;
               meta[stage] = m;
               const uint32_t dst = sbase + stage * Tr::kStageBytes;
               mbar_arrive_expect_tx(bar_full + 8 * stage, Tr::kStageBytes);
@@ -424,6 +441,13 @@ __global__ void __launch_bounds__(Traits<HD, KVB, NG>::kThreads, Traits<HD, KVB,
 #pragma unroll
     for (int mt = 0; mt < HD / 16; ++mt) acc[n][mt][0] = acc[n][mt][1] = acc[n][mt][2] = acc[n][mt][3] = 0.f;
 
+  // Queries of the next segment are copied (cp.async, 16 B) into a per-warp double buffer
+  // while the current segment streams, when q rows are 16-byte addressable.
+  const bool q_vec = (a.q_sd == 1) && (a.q_sh % 8 == 0) && (a.q_st % 8 == 0) &&
+                     ((reinterpret_cast<uintptr_t>(a.q) & 15) == 0);
+  uint8_t* qbuf = smem + Tr::kOffQ + warp * 2 * Tr::kQBufBytes;
+  int qslot = 0;
+  long long staged_row = -1;  // row whose q sits in qbuf[qslot ^ 1]
   // The first segment's token is known from the prologue: fetch its queries while the
   // first pages are still in flight.
   long long q_row = ctl->r0;
@@ -446,8 +470,44 @@ __global__ void __launch_bounds__(Traits<HD, KVB, NG>::kThreads, Traits<HD, KVB,
     const int h0 = (m.b * KVB + g) * group;
     if (m.flags & kFirst) {
       const long long row = static_cast<long long>(m.t) * d.nkvblk + m.b;
-      if (row != q_row) load_q_frags<HD, NG>(a, m.t, h0, group, lane, qa);
+      if (row == staged_row) {  // prefetched during the previous segment
+        asm volatile("cp.async.wait_all;" ::: "memory");
+        __syncwarp();
+        const uint8_t* qb = qbuf + (qslot ^ 1) * Tr::kQBufBytes;
+#pragma unroll
+        for (int kk = 0; kk < HD / 16; ++kk) {
+          const int d0 = kk * 16 + 2 * qd;
+          qa[kk][0] = r < group ? *reinterpret_cast<const uint32_t*>(qb + (r * HD + d0) * 2) : 0u;
+          qa[kk][1] = r < group ? *reinterpret_cast<const uint32_t*>(qb + (r * HD + d0 + 8) * 2) : 0u;
+          if (NG == 2) {
+            qa[kk][2 % (2 * NG)] =
+                r + 8 < group ? *reinterpret_cast<const uint32_t*>(qb + ((r + 8) * HD + d0) * 2) : 0u;
+            qa[kk][3 % (2 * NG)] =
+                r + 8 < group ? *reinterpret_cast<const uint32_t*>(qb + ((r + 8) * HD + d0 + 8) * 2) : 0u;
+          }
+        }
+      } else if (row != q_row) {
+        load_q_frags<HD, NG>(a, m.t, h0, group, lane, qa);
+      }
       q_row = -1;
+      staged_row = -1;
+      if (m.next_row >= 0 && q_vec) {  // start copying the next segment's queries
+        const long long nt = m.next_row / d.nkvblk;
+        const int nb = m.next_row % d.nkvblk;
+        const int nh0 = (nb * KVB + g) * group;
+        const int rows = min(group, Tr::kQRows);
+        uint8_t* dst = qbuf + qslot * Tr::kQBufBytes;
+        __syncwarp();
+        for (int c = lane; c < rows * (HD / 8); c += 32) {
+          const int rr = c / (HD / 8), cc = (c % (HD / 8)) * 8;
+          const __nv_bfloat16* src = a.q + nt * a.q_st + static_cast<long long>(nh0 + rr) * a.q_sh + cc;
+          asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(smem_u32(dst + (rr * HD + cc) * 2)),
+                       "l"(src) : "memory");
+        }
+        asm volatile("cp.async.commit_group;" ::: "memory");
+        staged_row = m.next_row;
+        qslot ^= 1;  // the buffer just filled is now qbuf[qslot ^ 1]
+      }
       m0 = m1 = -CUDART_INF_F;
       l0 = l1 = 0.f;
 #pragma unroll
