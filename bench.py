@@ -1,19 +1,30 @@
-"""Benchmark: ragged paged-attention decode on B200 (tok/s and achieved HBM bandwidth).
+"""Benchmark: ragged paged attention + slot-mapped KV append on B200.
 
-Workload (per GPU): the batch-64 decode configuration — 64 sequences, one query token each,
-contexts uniform in [128, 4096], Qwen2.5-3B GQA geometry (16 query heads, 2 KV heads,
-head_dim 128, scale 1/sqrt(128)), page size 16, pool = total pages x 1.1 + 8 scratch pages,
-block tables scattered by a seeded permutation, bf16 N(0,1) data.  One step = append the 64
-new K/V rows (Cache.write) + ragged_attention_direct over the batch.
+Default workload (the headline metric): batch-64 decode — 64 sequences per GPU, one query
+token each, contexts uniform in [128, 4096], Qwen2.5-3B GQA geometry (16 query heads, 2 KV
+heads, head_dim 128, scale 1/sqrt(128)), page size 16, pool = total pages x 1.1 + 8 scratch
+pages, block tables scattered by a seeded permutation, bf16 N(0,1) data.  One step = append
+the step's new K/V rows (Cache.write) + ragged_attention_direct over the batch.
 
-Multi-GPU (torchrun, one process per GPU): requests are sharded by context length (LPT) so
-every rank holds its requests' pages; no collective on the data path (weak scaling: 64
-requests per GPU).  Timing is on the device with CUDA events, max over ranks.
+Other workloads (`--workload`, one JSON line each; same timing rules):
+  mixed     8 prefill chunks x 512 tokens on cached context U[0, 2048] (causal inside the
+            chunk) + 56 decode rows with context U[256, 4096], one ragged launch per step
+  layers36  256 sequences (split over the GPUs) with context U[512, 8192]; one step = the
+            36 layers' append + attention, per-layer pools; q/k/v come from random-init
+            Qwen2.5-3B projections of N(0,1) hidden states with RoPE theta 1e6
+  tp2long   the reference's TP2 per-rank layout (8 query heads, 1 KV head): 32 sequences
+            with context U[16384, 32768] per TP2 pair (split over pairs on 4/8 GPUs), pool
+            filling ~60 % of HBM with scattered pages
 
-L2: each rank keeps R independent batches (own pool and tables, > 4x L2 in total) and
-rotates through them, so no step finds its pages in the 126 MB L2.
+Multi-GPU (torchrun, one process per GPU): requests are sharded by context (LPT), each rank
+holds its requests' pages, and no collective sits on the data path.  Timing is on the device
+with CUDA events, max over ranks.
 
-    python bench.py [--gpus N --steps K --warmup W] [--impl reference]
+L2: the decode64 and mixed workloads rotate R independent batches (own pool and tables,
+> 4x L2 in total), so no step finds its pages in the 126 MB L2; the other two workloads read
+pools far larger than L2 every step.
+
+    python bench.py [--gpus N --steps K --warmup W] [--workload W] [--impl reference]
 """
 from __future__ import annotations
 
@@ -38,6 +49,7 @@ SCALE = HEAD_DIM ** -0.5
 WORKLOAD = ("decode batch 64/GPU, ctx U[128,4096], 16q/2kv heads, d128, page 16, "
             "pool = pages x 1.1 + 8, scattered block tables, bf16 N(0,1)")
 FALLBACK_HBM_GBS = 6650.0
+FALLBACK_BF16_TFLOPS = 1590.0
 
 
 def parse():
@@ -46,10 +58,13 @@ def parse():
     p.add_argument("--steps", type=int, default=4000)
     p.add_argument("--warmup", type=int, default=200)
     p.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    p.add_argument("--workload", choices=["decode64", "mixed", "layers36", "tp2long"],
+                   default="decode64")
     p.add_argument("--replicas", type=int, default=4, help="batches rotated to defeat L2")
     p.add_argument("--graph-steps", type=int, default=100, help="steps per captured graph")
     p.add_argument("--e2e-steps", type=int, default=200)
     p.add_argument("--cpu-seconds", type=float, default=10.0)
+    p.add_argument("--pool-frac", type=float, default=0.6, help="tp2long pool share of HBM")
     p.add_argument("--seed", type=int, default=2024)
     return p.parse_args()
 
@@ -73,9 +88,9 @@ def peaks():
     try:
         with open(path) as f:
             d = json.load(f)
-        return float(d["hbm_gbs"]), "measured"
+        return float(d["hbm_gbs"]), float(d["bf16_tflops"]), "measured"
     except (OSError, KeyError, ValueError):
-        return FALLBACK_HBM_GBS, "fallback"
+        return FALLBACK_HBM_GBS, FALLBACK_BF16_TFLOPS, "fallback"
 
 
 class ClockSampler:
@@ -137,7 +152,8 @@ class ClockSampler:
 # ---------------------------------------------------------------------------------------
 def run_reference(args, rank, world):
     """Reference arm: the CPU restatement of the reference attention path (the reference is
-    pure Python/PyTorch and cannot run here), timed on this host's cores, rank 0 only."""
+    Python/PyTorch/Triton and its CPU path cannot travel here), timed on this host's cores,
+    rank 0 only."""
     if rank != 0:
         return
     import numpy as np
@@ -189,13 +205,14 @@ def run_reference(args, rank, world):
 def _cpu_batch(lengths, seed):
     import numpy as np
 
+    import oracle
+
     rng = np.random.default_rng(seed)
     pages = [math.ceil(L / 16) for L in lengths]
     data_pages = int(math.ceil(sum(pages) * 1.1))
     N = data_pages + 8
     perm = rng.permutation(data_pages).astype(np.int32)
-    W = max(pages)
-    bt = np.zeros((len(lengths), W), np.int32)
+    bt = np.zeros((len(lengths), max(pages)), np.int32)
     off = 0
     for i, n in enumerate(pages):
         bt[i, :n] = perm[off:off + n]
@@ -203,13 +220,10 @@ def _cpu_batch(lengths, seed):
     pos = np.asarray([L - 1 for L in lengths], np.int64)
     seq = np.arange(len(lengths), dtype=np.int32)
     slots = bt[seq, pos // 16].astype(np.int64) * 16 + pos % 16
-    f = lambda *s: rng.standard_normal(s, dtype=np.float32)
-    import oracle
-
-    r = oracle.bf16_round
-    return dict(kp=r(f(N, 16, KV_HEADS, HEAD_DIM)), vp=r(f(N, 16, KV_HEADS, HEAD_DIM)),
-                q=r(f(len(lengths), HEADS, HEAD_DIM)), kn=r(f(len(lengths), KV_HEADS, HEAD_DIM)),
-                vn=r(f(len(lengths), KV_HEADS, HEAD_DIM)), bt=bt, seq=seq, pos=pos, slots=slots)
+    f = lambda *s: oracle.bf16_round(rng.standard_normal(s, dtype=np.float32))
+    return dict(kp=f(N, 16, KV_HEADS, HEAD_DIM), vp=f(N, 16, KV_HEADS, HEAD_DIM),
+                q=f(len(lengths), HEADS, HEAD_DIM), kn=f(len(lengths), KV_HEADS, HEAD_DIM),
+                vn=f(len(lengths), KV_HEADS, HEAD_DIM), bt=bt, seq=seq, pos=pos, slots=slots)
 
 
 def cpu_baseline(args, lengths):
@@ -232,140 +246,321 @@ def cpu_baseline(args, lengths):
 
 
 # ---------------------------------------------------------------------------------------
-def run_ours(args, rank, world, dist):
+class Harness:
+    """Captures steps into CUDA graphs and times exactly K of them with CUDA events."""
+
+    def __init__(self, dev, dist, graph_steps):
+        import torch
+
+        self.torch = torch
+        self.dev = dev
+        self.dist = dist
+        self.S = max(1, graph_steps)
+        self.stream = torch.cuda.Stream(device=dev)
+
+    def barrier(self):
+        if self.dist is not None:
+            self.dist.barrier()
+        self.torch.cuda.synchronize()
+
+    def max_over_ranks(self, x):
+        if self.dist is None:
+            return x
+        t = self.torch.tensor([x], dtype=self.torch.float64, device=self.dev)
+        self.dist.all_reduce(t, op=self.dist.ReduceOp.MAX)
+        return float(t.item())
+
+    def sum_over_ranks(self, x):
+        if self.dist is None:
+            return x
+        t = self.torch.tensor([x], dtype=self.torch.float64, device=self.dev)
+        self.dist.all_reduce(t)
+        return float(t.item())
+
+    def capture(self, fns, n, start=0):
+        torch = self.torch
+        g = torch.cuda.CUDAGraph()
+        self.stream.wait_stream(torch.cuda.current_stream())
+        with torch.cuda.stream(self.stream):
+            with torch.cuda.graph(g, stream=self.stream):
+                for i in range(n):
+                    fns[(start + i) % len(fns)]()
+        torch.cuda.synchronize()
+        return g
+
+    def run_steps(self, fns, k, warm):
+        """Runs `warm` untimed then exactly `k` timed steps; returns device ms of the k."""
+        torch = self.torch
+        S = min(self.S, max(k, 1))
+        full = self.capture(fns, S)
+        rem = k % S
+        rem_g = self.capture(fns, rem, start=(k // S) * S) if rem else None
+        warm_full, warm_rem = divmod(warm, S)
+        warm_g = self.capture(fns, warm_rem) if warm_rem else None
+        with torch.cuda.stream(self.stream):
+            for _ in range(warm_full):
+                full.replay()
+            if warm_g is not None:
+                warm_g.replay()
+        self.barrier()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        t0 = time.monotonic()
+        with torch.cuda.stream(self.stream):
+            e0.record(self.stream)
+            for _ in range(k // S):
+                full.replay()
+            if rem_g is not None:
+                rem_g.replay()
+            e1.record(self.stream)
+        self.barrier()
+        t1 = time.monotonic()
+        return e0.elapsed_time(e1), (t0, t1)
+
+    def per_launch_ms(self, fns, n):
+        """Mean device time of one call of each fn, from graph-captured per-launch events."""
+        torch = self.torch
+        n = max(1, n)
+        # external=True: the records become event-record nodes of the graph, so each replay
+        # timestamps every launch on the stream it runs on.
+        ev = [(torch.cuda.Event(enable_timing=True, external=True),
+               torch.cuda.Event(enable_timing=True, external=True)) for _ in range(n)]
+        g = torch.cuda.CUDAGraph()
+        self.stream.wait_stream(torch.cuda.current_stream())
+        with torch.cuda.stream(self.stream):
+            with torch.cuda.graph(g, stream=self.stream):
+                for i in range(n):
+                    ev[i][0].record(self.stream)
+                    fns[i % len(fns)]()
+                    ev[i][1].record(self.stream)
+        for _ in range(2):
+            with torch.cuda.stream(self.stream):
+                g.replay()
+            torch.cuda.synchronize()
+        return statistics.mean(a.elapsed_time(b) for a, b in ev)
+
+
+def run_decode64(args, rank, world, dist, h):
     import torch
 
     import shardserve_b200 as sb
     from shardserve_b200 import kernel as K
     from shardserve_b200.workloads import append_bytes, attention_bytes, decode_batch
 
-    dev = torch.device("cuda", torch.cuda.current_device())
+    dev = h.dev
     lengths = rank_lengths(world, rank, args.seed)
     T = len(lengths)
     R = max(1, args.replicas)
     batches = [decode_batch(lengths, HEADS, KV_HEADS, HEAD_DIM, seed=args.seed + 1000 * rank + r,
                             device=dev) for r in range(R)]
 
-    def step(b):
-        sb.kv_append(b.k_pool, b.v_pool, b.k_new, b.v_new, b.slots)
-        return sb.ragged_attention_direct(b.q, b.k_pool, b.v_pool, b.block_tables, b.seq_ids,
-                                          b.positions, SCALE)
+    def step_fn(b):
+        def f():
+            sb.kv_append(b.k_pool, b.v_pool, b.k_new, b.v_new, b.slots)
+            sb.ragged_attention_direct(b.q, b.k_pool, b.v_pool, b.block_tables, b.seq_ids,
+                                       b.positions, SCALE)
+        return f
 
-    # Warm the workspace and check the fast path is the one that runs.
+    def attn_fn(b):
+        return lambda: sb.ragged_attention_direct(b.q, b.k_pool, b.v_pool, b.block_tables,
+                                                  b.seq_ids, b.positions, SCALE)
+
     for b in batches:
-        step(b)
+        step_fn(b)()
     torch.cuda.synchronize()
     assert K.last_attention_path() == 1, "attention did not take the TMA tensor-core path"
     assert K.device_errors(dev) == 0
 
-    S = max(R, (args.graph_steps // R) * R)
-    stream = torch.cuda.Stream(device=dev)
-    stream.wait_stream(torch.cuda.current_stream())
-    outs = []
-    with torch.cuda.stream(stream):
-        g_full = torch.cuda.CUDAGraph()
-        with torch.cuda.graph(g_full, stream=stream):
-            for i in range(S):
-                outs.append(step(batches[i % R]))
-        g_attn = torch.cuda.CUDAGraph()
-        # external=True: the records become event-record nodes of the graph, so each replay
-        # timestamps every attention launch on the stream it runs on.
-        ev = [(torch.cuda.Event(enable_timing=True, external=True),
-               torch.cuda.Event(enable_timing=True, external=True)) for _ in range(S)]
-        with torch.cuda.graph(g_attn, stream=stream):
-            for i in range(S):
-                b = batches[i % R]
-                ev[i][0].record(stream)
-                sb.ragged_attention_direct(b.q, b.k_pool, b.v_pool, b.block_tables, b.seq_ids,
-                                           b.positions, SCALE)
-                ev[i][1].record(stream)
-    torch.cuda.synchronize()
-
-    def barrier():
-        if dist is not None:
-            dist.barrier()
-        torch.cuda.synchronize()
-
-    def max_over_ranks(x):
-        if dist is None:
-            return x
-        t = torch.tensor([x], dtype=torch.float64, device=dev)
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        return float(t.item())
-
-    reps_w = max(1, math.ceil(args.warmup / S))
-    reps = max(1, math.ceil(args.steps / S))
-    steps = reps * S
     clocks = ClockSampler(dev.index)
     clocks.start()
     time.sleep(0.3)
-    with torch.cuda.stream(stream):
-        for _ in range(reps_w):
-            g_full.replay()
-    barrier()
-    # ---- timed region: exactly `steps` steps (append + attention) ----------------------
-    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    t_wall0 = time.monotonic()
-    with torch.cuda.stream(stream):
-        e0.record(stream)
-        for _ in range(reps):
-            g_full.replay()
-        e1.record(stream)
-    barrier()
-    t_wall1 = time.monotonic()
-    ms_rank = e0.elapsed_time(e1)
-    # ---- attention kernel alone, one CUDA-event pair per launch --------------------------
-    with torch.cuda.stream(stream):
-        g_attn.replay()
-    torch.cuda.synchronize()
-    with torch.cuda.stream(stream):
-        g_attn.replay()
-    torch.cuda.synchronize()
-    kernel_ms = statistics.mean(a.elapsed_time(b) for a, b in ev)
+    steps = [step_fn(b) for b in batches]
+    ms, (t0, t1) = h.run_steps(steps, args.steps, args.warmup)
+    kernel_ms = h.per_launch_ms([attn_fn(b) for b in batches], min(args.graph_steps, 200))
     clocks.stop()
-    ms = max_over_ranks(ms_rank)
-    kernel_ms = max_over_ranks(kernel_ms)
-    tok_all = torch.tensor([float(T)], dtype=torch.float64, device=dev)
-    if dist is not None:
-        dist.all_reduce(tok_all)
-    tokens_per_step = float(tok_all.item())
-    value = tokens_per_step * steps / (ms / 1e3)
-
-    # ---- end to end through the public API with host buffers ---------------------------
-    e2e = run_e2e(args, batches[0], dev, dist, barrier, max_over_ranks, tok_all.item())
-
+    ms = h.max_over_ranks(ms)
+    kernel_ms = h.max_over_ranks(kernel_ms)
+    tokens_all = h.sum_over_ranks(float(T))
+    value = tokens_all * args.steps / (ms / 1e3)
+    e2e = run_e2e(args, batches[0], dev, h, tokens_all)
     abytes = attention_bytes(lengths, HEADS, KV_HEADS, HEAD_DIM)
-    peak, peak_kind = peaks()
+    peak, _, peak_kind = peaks()
     achieved = abytes / (kernel_ms / 1e3) / 1e9
-    traffic = traffic_from_profile(abytes)
     line = {
-        "metric": METRIC, "value": value, "unit": "tok/s", "n_gpus": world, "steps": steps,
-        "warmup": reps_w * S, "ms_per_step": ms / steps, "higher_is_better": True,
+        "metric": METRIC, "value": value, "unit": "tok/s", "n_gpus": world, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": ms / args.steps, "higher_is_better": True,
         "scaling": "weak", "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
         "config": {"workload": WORKLOAD, "tokens_per_gpu_step": T,
                    "parallelism": f"request-sharded x{world} (LPT by context), no collective",
                    "l2": f"{R} rotating batches of ~{abytes / 1e6:.0f} MB each per GPU (> L2)",
-                   "graph": f"{S} steps per CUDA graph, {reps} replays"},
+                   "graph": f"{min(args.graph_steps, args.steps)} steps per CUDA graph"},
         "hbm_tbs": achieved / 1e3,
         "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
-                     "frac": achieved / peak, "traffic": traffic,
-                     "kernel": "decode_attention_kernel<128,2>",
+                     "frac": achieved / peak, "traffic": traffic_from_profile(),
+                     "kernel": "decode_attention_kernel<128,2,1> + merge_partials_kernel<128,2>",
                      "kernel_us": kernel_ms * 1e3, "algorithmic_bytes": abytes,
                      "peak_kind": f"{peak_kind} copy bandwidth"},
         "append_bytes": append_bytes(T, KV_HEADS, HEAD_DIM),
         "e2e": e2e,
-        "gpu_launches": 2 * steps,
-        "clocks": clocks.summary(t_wall0, t_wall1),
+        "gpu_launches": 3 * args.steps,
+        "clocks": clocks.summary(t0, t1),
     }
-    if rank == 0 and world == 1:
-        line["cpu_baseline"] = cpu_baseline(args, lengths)
-    elif rank == 0:
-        line["cpu_baseline"] = None
-    del g_full, g_attn
+    if rank == 0:
+        line["cpu_baseline"] = cpu_baseline(args, lengths) if world == 1 else None
     return line
 
 
-def run_e2e(args, b, dev, dist, barrier, max_over_ranks, tokens_all):
+def run_mixed(args, rank, world, dist, h):
+    """8 prefill chunks x 512 tokens on cached context U[0, 2048] + 56 decode rows with
+    context U[256, 4096] (decode rows first, as the reference scheduler packs them)."""
+    import torch
+
+    import shardserve_b200 as sb
+    from shardserve_b200.workloads import attention_bytes, prefill_flops, ragged_batch
+
+    g = torch.Generator().manual_seed(args.seed + rank)
+    decode = [(int(c) - 1, 1) for c in torch.randint(256, 4097, (56,), generator=g)]
+    prefill = [(int(c), 512) for c in torch.randint(0, 2049, (8,), generator=g)]
+    rows = decode + prefill
+    R = max(1, args.replicas)
+    batches = [ragged_batch(rows, HEADS, KV_HEADS, HEAD_DIM, seed=args.seed + 7 * r + rank,
+                            device=h.dev) for r in range(R)]
+    T = batches[0].tokens
+
+    def step_fn(b):
+        def f():
+            sb.kv_append(b.k_pool, b.v_pool, b.k_new, b.v_new, b.slots)
+            sb.ragged_attention_direct(b.q, b.k_pool, b.v_pool, b.block_tables, b.seq_ids,
+                                       b.positions, SCALE)
+        return f
+
+    for b in batches:
+        step_fn(b)()
+    torch.cuda.synchronize()
+    ms, (t0, t1) = h.run_steps([step_fn(b) for b in batches], args.steps, args.warmup)
+    ms = h.max_over_ranks(ms)
+    step_s = ms / 1e3 / args.steps
+    flops = prefill_flops(prefill, HEADS, HEAD_DIM)
+    dbytes = attention_bytes([c + n for c, n in decode], HEADS, KV_HEADS, HEAD_DIM)
+    _, tflops_peak, kind = peaks()
+    return {"metric": "mixed chunked-prefill + decode query tok/s", "workload": "mixed",
+            "value": h.sum_over_ranks(T) / step_s, "unit": "tok/s", "n_gpus": world,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms / args.steps,
+            "tokens_per_gpu_step": T, "prefill_tflops_per_step": flops / 1e12,
+            "prefill_tflops_achieved": flops / step_s / 1e12,
+            "tensor_frac_of_peak": flops / step_s / 1e12 / tflops_peak,
+            "decode_bytes_per_step": dbytes, "peak_kind": kind, "dtype": "bf16",
+            "data": "synthetic", "scaling": "weak"}
+
+
+def run_layers36(args, rank, world, dist, h):
+    """36 layers of decode attention for 256 sequences (split over the GPUs): q/k/v from
+    random-init projections of N(0,1) hidden states with RoPE (theta 1e6)."""
+    import torch
+    import torch.nn.functional as F
+
+    import shardserve_b200 as sb
+    from shardserve_b200.sharding import shard_requests
+    from shardserve_b200.workloads import attention_bytes, ragged_batch, uniform_lengths
+
+    layers, hidden = 36, 2048
+    lengths = uniform_lengths(256, 512, 8192, args.seed)
+    mine = [lengths[i] for i in shard_requests(lengths, world)[rank]]
+    b = ragged_batch([(L - 1, 1) for L in mine], HEADS, KV_HEADS, HEAD_DIM, seed=args.seed + rank,
+                     device=h.dev, layers=layers)
+    T = b.tokens
+    dev = h.dev
+    gen = torch.Generator(device=dev).manual_seed(args.seed + 99)
+    x = torch.randn(T, hidden, generator=gen, device=dev).to(torch.bfloat16)
+    inv = 1.0 / (1e6 ** (torch.arange(0, HEAD_DIM, 2, device=dev, dtype=torch.float32) / HEAD_DIM))
+    ang = b.positions.float()[:, None] * inv[None, :]
+    cos, sin = torch.cat([ang, ang], -1).cos()[:, None], torch.cat([ang, ang], -1).sin()[:, None]
+
+    def rope(t):
+        half = t.shape[-1] // 2
+        rot = torch.cat((-t[..., half:], t[..., :half]), -1)
+        return (t.float() * cos + rot.float() * sin).to(torch.bfloat16)
+
+    qs, ks, vs = [], [], []
+    for _ in range(layers):
+        w = lambda o: (torch.randn(o, hidden, generator=gen, device=dev) * hidden ** -0.5).to(torch.bfloat16)
+        bias = lambda o: (torch.randn(o, generator=gen, device=dev) * 0.02).to(torch.bfloat16)
+        q = F.linear(x, w(HEADS * HEAD_DIM), bias(HEADS * HEAD_DIM)).view(T, HEADS, HEAD_DIM)
+        k = F.linear(x, w(KV_HEADS * HEAD_DIM), bias(KV_HEADS * HEAD_DIM)).view(T, KV_HEADS, HEAD_DIM)
+        v = F.linear(x, w(KV_HEADS * HEAD_DIM), bias(KV_HEADS * HEAD_DIM)).view(T, KV_HEADS, HEAD_DIM)
+        qs.append(rope(q).contiguous())
+        ks.append(rope(k).contiguous())
+        vs.append(v.contiguous())
+
+    def step():
+        for l in range(layers):
+            sb.kv_append(b.k_pool[l], b.v_pool[l], ks[l], vs[l], b.slots)
+            sb.ragged_attention_direct(qs[l], b.k_pool[l], b.v_pool[l], b.block_tables,
+                                       b.seq_ids, b.positions, SCALE)
+
+    step()
+    torch.cuda.synchronize()
+    k = max(1, args.steps // layers)
+    w = max(1, args.warmup // layers)
+    h.S = min(h.S, 4)
+    ms, _ = h.run_steps([step], k, w)
+    ms = h.max_over_ranks(ms)
+    step_s = ms / 1e3 / k
+    abytes = attention_bytes(mine, HEADS, KV_HEADS, HEAD_DIM) * layers
+    peak, _, kind = peaks()
+    achieved = h.sum_over_ranks(abytes) / world / step_s / 1e9
+    return {"metric": "36-layer decode-step attention tok/s", "workload": "layers36",
+            "value": h.sum_over_ranks(T) / step_s, "unit": "tok/s", "n_gpus": world,
+            "steps": k, "warmup": w, "ms_per_step": ms / k, "tokens_per_gpu_step": T,
+            "bytes_per_gpu_step": abytes, "hbm_gbs_per_gpu": achieved,
+            "hbm_frac": achieved / peak, "peak_kind": kind, "dtype": "bf16",
+            "data": "synthetic (random-init projections)", "scaling": "strong"}
+
+
+def run_tp2long(args, rank, world, dist, h):
+    """TP2 per-rank layout (8 q heads, 1 KV head), 32 sequences of context U[16384, 32768]
+    per TP2 pair, split over pairs; pool ~60 % of HBM, scattered pages."""
+    import torch
+
+    import shardserve_b200 as sb
+    from shardserve_b200.sharding import shard_requests
+    from shardserve_b200.workloads import attention_bytes, ragged_batch, uniform_lengths
+
+    pairs = max(1, world // 2)
+    pair = rank // 2 if world >= 2 else 0
+    lengths = uniform_lengths(32, 16384, 32768, args.seed)
+    mine = [lengths[i] for i in shard_requests(lengths, pairs)[pair]]
+    free, _ = torch.cuda.mem_get_info(h.dev)
+    page_bytes = 2 * 16 * 1 * HEAD_DIM * 2
+    pool_pages = int(free * args.pool_frac / page_bytes)
+    b = ragged_batch([(L - 1, 1) for L in mine], 8, 1, HEAD_DIM, seed=args.seed + rank,
+                     device=h.dev, pool_pages=pool_pages)
+    T = b.tokens
+
+    def step():
+        sb.kv_append(b.k_pool, b.v_pool, b.k_new, b.v_new, b.slots)
+        sb.ragged_attention_direct(b.q, b.k_pool, b.v_pool, b.block_tables, b.seq_ids,
+                                   b.positions, SCALE)
+
+    step()
+    torch.cuda.synchronize()
+    ms, _ = h.run_steps([step], args.steps, args.warmup)
+    ms = h.max_over_ranks(ms)
+    step_s = ms / 1e3 / args.steps
+    abytes = attention_bytes(mine, 8, 1, HEAD_DIM)
+    peak, _, kind = peaks()
+    achieved = abytes / step_s / 1e9
+    # A decode token of a TP2 pair is complete when both ranks did their halves.
+    seqs_all = 32 if world >= 2 else T
+    return {"metric": "TP2 long-context decode tok/s", "workload": "tp2long",
+            "value": seqs_all / step_s, "unit": "tok/s", "n_gpus": world, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": ms / args.steps,
+            "seqs_per_rank": T, "pool_gb": 2 * b.k_pool.numel() * 2 / 1e9,
+            "bytes_per_rank_step": abytes, "hbm_gbs_per_rank": achieved,
+            "hbm_frac": achieved / peak, "peak_kind": kind, "dtype": "bf16",
+            "data": "synthetic", "scaling": "strong"}
+
+
+def run_e2e(args, b, dev, h, tokens_all):
     """Per step: pinned host -> device copies of q, new K/V rows, positions, sequence ids,
     block tables and slots; Cache.write + ragged_attention_direct through the public API;
     device -> pinned host copy of the output; stream synchronise (the reference runtime reads
@@ -393,29 +588,32 @@ def run_e2e(args, b, dev, dist, barrier, max_over_ranks, tokens_all):
 
     for _ in range(20):
         one()
-    barrier()
+    h.barrier()
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     e0.record(stream)
     for _ in range(args.e2e_steps):
         one()
     e1.record(stream)
-    barrier()
-    ms = max_over_ranks(e0.elapsed_time(e1))
+    h.barrier()
+    ms = h.max_over_ranks(e0.elapsed_time(e1))
     return {"value": tokens_all * args.e2e_steps / (ms / 1e3), "unit": "tok/s",
             "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
             "ms_per_step": ms / args.e2e_steps,
             "api": "shardserve_b200.kv_append + ragged_attention_direct, eager, per-step sync"}
 
 
-def traffic_from_profile(abytes):
-    """DRAM bytes per launch from the committed ncu summary, if one exists."""
+def traffic_from_profile():
+    """DRAM bytes per launch of the decode kernel from the committed ncu summary."""
     path = os.path.join(ROOT, "profiles", "decode_attention_batch64.json")
     try:
         with open(path) as f:
-            d = json.load(f)
-        return d["dram_bytes_per_launch"]
+            return json.load(f)["dram_bytes_per_launch"]
     except (OSError, KeyError, ValueError):
         return None
+
+
+RUNNERS = {"decode64": run_decode64, "mixed": run_mixed, "layers36": run_layers36,
+           "tp2long": run_tp2long}
 
 
 def main():
@@ -441,7 +639,8 @@ def main():
     else:
         torch.cuda.set_device(0)
     try:
-        line = run_ours(args, rank, world, dist)
+        h = Harness(torch.device("cuda", torch.cuda.current_device()), dist, args.graph_steps)
+        line = RUNNERS[args.workload](args, rank, world, dist, h)
         if rank == 0:
             print(json.dumps(line), flush=True)
     finally:
