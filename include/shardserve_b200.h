@@ -156,7 +156,8 @@ SS_API int ss_fetch_device_errors(void* workspace, int clear, uint32_t* flags, v
 /*
  * Which kernel family the last successful ss_ragged_paged_attention call on this thread
  * used: 1 = TMA/tensor-core split-K kernel, 2 = generic strided kernel (layouts the TMA
- * path cannot describe), 0 = none yet.  Lets tests assert the fast path really ran.
+ * path cannot describe), 3 = split-K kernel for isolated tokens plus tcgen05 tiles for the
+ * chunked-prefill runs, 0 = none yet.  Lets tests assert the fast path really ran.
  */
 SS_API int ss_last_attention_path(void);
 

@@ -16,7 +16,8 @@ REPO_DIR = os.path.dirname(PKG_DIR)
 CSRC = os.path.join(PKG_DIR, "csrc")
 LIB_NAME = "libshardserve_b200.so"
 LIB_PATH = os.path.join(PKG_DIR, LIB_NAME)
-SOURCES = ["capi.cu", "decode_attention.cu", "generic_attention.cu", "kv_append.cu", "noalloc.cu"]
+SOURCES = ["capi.cu", "decode_attention.cu", "generic_attention.cu", "kv_append.cu", "noalloc.cu",
+           "prefill_attention.cu"]
 HEADERS = ["attention.cuh", "ptx.cuh"]
 
 NVCC_FLAGS = [

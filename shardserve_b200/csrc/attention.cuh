@@ -130,6 +130,14 @@ cudaError_t launch_merge(const DecodeGeometry& g, const DecodeArgs& d, cudaStrea
 
 cudaError_t launch_generic_attention(const AttnArgs& a, cudaStream_t stream);
 
+// tcgen05 chunked-prefill tiles (prefill_attention.cu): layouts the tile kernel handles,
+// the run length that makes a token a prefill token, and the launch (programmatic
+// dependent launch after the decode kernel).
+bool prefill_supported(const AttnArgs& a);
+int prefill_min_run();
+cudaError_t launch_prefill(const CUtensorMap& tmQ, const CUtensorMap& tmK, const CUtensorMap& tmV,
+                           const AttnArgs& a, cudaStream_t stream);
+
 struct AppendArgs {
   const __nv_bfloat16* k;
   long long k_st, k_sh, k_sd;

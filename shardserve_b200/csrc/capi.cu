@@ -56,17 +56,37 @@ EncodeTiledFn encode_fn() {
 // of `kvb` heads laid out as [head][d / 64][key][d % 64] in shared memory with the 128-byte
 // swizzle: each 128-byte line holds 64 values of one key, and the 8 keys an ldmatrix reads
 // fall in 8 different swizzle phases (bank-conflict free).
+// `dhalves` = 64-dim halves per box: D / 64 for the decode kernel (whole page of `kvb` heads),
+// 1 for the prefill tiles (one half of one head per box).
 bool encode_pool_map(CUtensorMap* map, const void* base, long long N, int KVH, int D,
-                     const int64_t* st, int kvb) {
+                     const int64_t* st, int kvb, int dhalves) {
   EncodeTiledFn fn = encode_fn();
   if (!fn) return false;
   cuuint64_t dims[5] = {64, 16, static_cast<cuuint64_t>(D / 64), static_cast<cuuint64_t>(KVH),
                         static_cast<cuuint64_t>(N)};
   cuuint64_t strides[4] = {static_cast<cuuint64_t>(st[1]) * 2, 64 * 2,
                            static_cast<cuuint64_t>(st[2]) * 2, static_cast<cuuint64_t>(st[0]) * 2};
-  cuuint32_t box[5] = {64, 16, static_cast<cuuint32_t>(D / 64), static_cast<cuuint32_t>(kvb), 1};
+  cuuint32_t box[5] = {64, 16, static_cast<cuuint32_t>(dhalves), static_cast<cuuint32_t>(kvb), 1};
   cuuint32_t estr[5] = {1, 1, 1, 1, 1};
   const CUresult r = fn(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 5, const_cast<void*>(base), dims,
+                        strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                        CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                        CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS;
+}
+
+// q [T, H, D] as (d % 64, d / 64, head, token) with a box of 64 dims x 8 heads x 16 tokens
+// for the prefill tiles (rows = token * 8 + head, 128-byte swizzle).
+bool encode_q_map(CUtensorMap* map, const void* q, long long T, int H, int D, const int64_t* st) {
+  EncodeTiledFn fn = encode_fn();
+  if (!fn) return false;
+  cuuint64_t dims[4] = {64, static_cast<cuuint64_t>(D / 64), static_cast<cuuint64_t>(H),
+                        static_cast<cuuint64_t>(T)};
+  cuuint64_t strides[3] = {64 * 2, static_cast<cuuint64_t>(st[1]) * 2,
+                           static_cast<cuuint64_t>(st[0]) * 2};
+  cuuint32_t box[4] = {64, 1, 8, 16};
+  cuuint32_t estr[4] = {1, 1, 1, 1};
+  const CUresult r = fn(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 4, const_cast<void*>(q), dims,
                         strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
                         CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
                         CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
@@ -246,22 +266,38 @@ int ss_ragged_paged_attention(const void* q, const int64_t q_strides[3], const v
     if (workspace_bytes < need)
       return fail(SS_ERR_WORKSPACE, "workspace holds %zu bytes, %zu needed", workspace_bytes, need);
     CUtensorMap tmK, tmV;
-    if (encode_pool_map(&tmK, k_pool, num_pages, kv_heads, head_dim, k_pool_strides, g.kvb) &&
-        encode_pool_map(&tmV, v_pool, num_pages, kv_heads, head_dim, v_pool_strides, g.kvb)) {
+    if (encode_pool_map(&tmK, k_pool, num_pages, kv_heads, head_dim, k_pool_strides, g.kvb,
+                        head_dim / 64) &&
+        encode_pool_map(&tmV, v_pool, num_pages, kv_heads, head_dim, v_pool_strides, g.kvb,
+                        head_dim / 64)) {
+      // Chunked-prefill tiles when the batch must hold a multi-token run (more query tokens
+      // than sequence rows) and the layout suits the tile kernel; otherwise the split-K
+      // kernel computes every token.
+      CUtensorMap tmQ, tmKp, tmVp;
+      const bool prefill = tokens > bt_rows && ss::prefill_supported(a) &&
+                           encode_q_map(&tmQ, q, tokens, heads, head_dim, q_strides) &&
+                           encode_pool_map(&tmKp, k_pool, num_pages, kv_heads, head_dim,
+                                           k_pool_strides, 1, 1) &&
+                           encode_pool_map(&tmVp, v_pool, num_pages, kv_heads, head_dim,
+                                           v_pool_strides, 1, 1);
       ss::DecodeArgs d;
       d.a = a;
       d.kvb = g.kvb;
       d.nkvblk = g.nkvblk;
       d.G = g.G;
-      d.min_run = 0;
+      d.min_run = prefill ? ss::prefill_min_run() : 0;
       uint8_t* ws = static_cast<uint8_t*>(workspace);
       d.part = reinterpret_cast<float*>(ws + ss::kWsHeader);
       d.desc = reinterpret_cast<int4*>(ws + ss::kWsHeader + g.part_bytes);
       e = ss::launch_decode(g, tmK, tmV, d, s);
       if (e != cudaSuccess) return cuda_fail(e, "decode attention launch");
+      if (prefill) {
+        e = ss::launch_prefill(tmQ, tmKp, tmVp, a, s);
+        if (e != cudaSuccess) return cuda_fail(e, "prefill attention launch");
+      }
       e = ss::launch_merge(g, d, s);
       if (e != cudaSuccess) return cuda_fail(e, "split-K merge launch");
-      g_last_path = 1;
+      g_last_path = prefill ? 3 : 1;
       return SS_OK;
     }
   }

@@ -263,7 +263,10 @@ __global__ void __launch_bounds__(Traits<HD, KVB, NG>::kThreads, Traits<HD, KVB,
     if (a.T <= CH) U = total;  // single pass: the scan also gives the total
     chunk = max((U + d.G - 1) / d.G, static_cast<long long>(kMinChunk));
     u0 = static_cast<long long>(blockIdx.x) * chunk;
-    if (u0 >= U) return;  // uniform across the CTA
+    if (u0 >= U) {  // uniform across the CTA; see the wait/trigger order below
+      griddep_wait();
+      return;
+    }
 #pragma unroll
     for (int i = 0; i < ITEMS; ++i) {
       if (us[i] > 0 && start <= u0 && u0 < start + us[i]) {
@@ -280,10 +283,14 @@ __global__ void __launch_bounds__(Traits<HD, KVB, NG>::kThreads, Traits<HD, KVB,
     if (ctl->found) break;
   }
   __syncthreads();
-  if (!ctl->found) return;  // cannot happen when u0 < U; uniform across the CTA
+  if (!ctl->found) {  // cannot happen when u0 < U; uniform across the CTA
+    griddep_wait();
+    return;
+  }
   const int n_units = static_cast<int>(min(chunk, U - u0));
-  // The merge kernel that follows may be scheduled now; it waits for this grid to finish.
-  griddep_launch_dependents();
+  // Order of programmatic-launch operations: every CTA waits for the preceding grid (the
+  // KV append) before it lets the next grid (prefill tiles or the split-K merge) start, so
+  // a dependent grid that starts reads pool pages the append has finished writing.
   if (warp == Tr::kNCW) {
     // ============================ producer warp ====================================
     const uint64_t policy = l2_policy_evict_first();
@@ -310,6 +317,7 @@ __global__ void __launch_bounds__(Traits<HD, KVB, NG>::kThreads, Traits<HD, KVB,
     // From here on the pool pages (appended by the preceding kernel) and the workspace
     // are touched.
     griddep_wait();
+    griddep_launch_dependents();
     while (remaining > 0 && ok) {
       const long long t = r / d.nkvblk;
       const int b = static_cast<int>(r % d.nkvblk);
@@ -422,6 +430,7 @@ __global__ void __launch_bounds__(Traits<HD, KVB, NG>::kThreads, Traits<HD, KVB,
 
   // ============================== consumer warps ======================================
   griddep_wait();
+  griddep_launch_dependents();
   const int g = warp >> 1;  // KV head inside the block
   const int j = warp & 1;   // page parity this warp computes
   const int r = lane >> 2, qd = lane & 3;

@@ -83,7 +83,8 @@ def device_errors(device, clear: bool = True) -> int:
 
 
 def last_attention_path() -> int:
-    """1 = TMA tensor-core split-K kernel, 2 = generic strided kernel, 0 = none yet."""
+    """1 = TMA tensor-core split-K kernel, 2 = generic strided kernel, 3 = split-K kernel
+    plus tcgen05 chunked-prefill tiles, 0 = none yet."""
     return _native.lib().ss_last_attention_path()
 
 

@@ -40,6 +40,16 @@ def to_device(inp, dev, pos_dtype=torch.int64, seq_dtype=torch.int32, bt_dtype=t
     return t
 
 
+def expected_path(inp):
+    """2: generic kernel; 3: split-K + tcgen05 prefill tiles (more tokens than rows, 8 query
+    heads per KV head, head_dim 128); 1: split-K only."""
+    group = inp["H"] // inp["KVH"]
+    if group > 16:
+        return 2
+    T, B = len(inp["seq_ids"]), inp["block_tables"].shape[0]
+    return 3 if (T > B and group == 8 and inp["D"] == 128) else 1
+
+
 def run(inp, t, q=None, kp=None, vp=None):
     kp = t["kp"] if kp is None else kp
     vp = t["vp"] if vp is None else vp
@@ -73,8 +83,7 @@ def test_golden_case(name, dev):
     ref = oracle.ragged_attention(q, kp, vp, inp["block_tables"], inp["seq_ids"],
                                   inp["positions"], inp["scale"])
     check_close(out, ref)
-    group = inp["H"] // inp["KVH"]
-    assert K.last_attention_path() == (1 if group <= 16 else 2)
+    assert K.last_attention_path() == expected_path(inp)
     assert K.device_errors(dev) == 0
 
 
@@ -114,7 +123,7 @@ def test_strided_query_output_and_pool_views(dev):
     vlayers = torch.zeros_like(layers)
     vlayers[1].copy_(t2["vp"])
     out = run(inp, t2, q=qv, kp=layers[1], vp=vlayers[1])
-    assert K.last_attention_path() == 1
+    assert K.last_attention_path() == expected_path(inp)
     assert torch.equal(out, base)
     t3 = to_device(inp, dev)
     N, P, KVH, _ = t3["kp"].shape
@@ -123,7 +132,7 @@ def test_strided_query_output_and_pool_views(dev):
     padk[..., :D] = t3["kp"]
     padv[..., :D] = t3["vp"]
     out3 = run(inp, t3, kp=padk[..., :D], vp=padv[..., :D])
-    assert K.last_attention_path() == 1
+    assert K.last_attention_path() == expected_path(inp)
     assert torch.equal(out3, base)
 
 
@@ -295,3 +304,48 @@ def test_mixed_geometries_share_one_workspace(dev):
         inp = cases.build(name)
         want, _ = load_golden(name)
         check_close(run(inp, to_device(inp, dev)), want)
+
+
+def _ragged_rows_case(dev, rows, H, KVH, seed):
+    """Device + oracle inputs for (cached context, query tokens) rows, appended first."""
+    from shardserve_b200.workloads import ragged_batch
+
+    b = ragged_batch(rows, H, KVH, 128, seed=seed, device=dev)
+    sb.kv_append(b.k_pool, b.v_pool, b.k_new, b.v_new, b.slots)
+    out = sb.ragged_attention_direct(b.q, b.k_pool, b.v_pool, b.block_tables, b.seq_ids,
+                                     b.positions, 128 ** -0.5)
+    path = K.last_attention_path()
+    f = lambda x: x.float().cpu().numpy()
+    ref = oracle.ragged_attention(f(b.q), f(b.k_pool), f(b.v_pool), b.block_tables.cpu().numpy(),
+                                  b.seq_ids.cpu().numpy(), b.positions.cpu().numpy(), 128 ** -0.5,
+                                  threads=oracle.host_threads())
+    return out, ref, path
+
+
+def test_prefill_tiles_with_short_runs_and_window_straddles(dev):
+    """Runs of 2..20 tokens packed so one 16-token tile window holds several runs (and a
+    decode row), runs cross tile boundaries, and contexts cross 128-key blocks."""
+    rows = [(10, 3), (50, 5), (0, 7), (200, 1), (100, 2), (33, 20), (127, 2), (128, 16), (0, 1)]
+    out, ref, path = _ragged_rows_case(dev, rows, 16, 2, seed=31)
+    assert path == 3
+    check_close(out, ref)
+    assert K.device_errors(dev) == 0
+
+
+def test_prefill_tiles_config3_shape_against_oracle(dev):
+    """Mixed chunked-prefill batch of the benchmark's shape (reduced: 4 chunks of 512 on
+    cached context up to 2048 and 16 decode rows) against the CPU oracle."""
+    g = torch.Generator().manual_seed(3)
+    decode = [(int(c) - 1, 1) for c in torch.randint(256, 4097, (16,), generator=g)]
+    prefill = [(int(c), 512) for c in torch.randint(0, 2049, (4,), generator=g)]
+    out, ref, path = _ragged_rows_case(dev, decode + prefill, 16, 2, seed=32)
+    assert path == 3
+    check_close(out, ref)
+    assert K.device_errors(dev) == 0
+
+
+def test_prefill_tiles_tp2_layout_against_oracle(dev):
+    """TP2 per-rank heads (8 query heads, 1 KV head) with a 300-token chunk on 1000 cached."""
+    out, ref, path = _ragged_rows_case(dev, [(1000, 300), (4000, 1), (5, 40)], 8, 1, seed=33)
+    assert path == 3
+    check_close(out, ref)
