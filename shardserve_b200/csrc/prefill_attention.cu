@@ -5,22 +5,38 @@
 // tokens of one sequence (a chunked-prefill chunk; token_in_long_run with min_run 2) are
 // computed here as dense tiles; isolated tokens (decode rows) by the split-K decode kernel.
 //
-// Tile: 16 consecutive query tokens x the 8 query heads of one KV head = 128 rows (M), head
-// dim 128 (K), keys in blocks of 128 (N).  Per key block:
-//   S  = Q.K^T       tcgen05.mma kind::f16, A = Q (smem, K-major), B = K (smem, K-major)
-//                    -> 128 x 128 fp32 in TMEM columns [0, 128)
-//   softmax          one thread per TMEM lane (= tile row): causal mask from the token's
-//                    position, base-2 online softmax; O is rescaled in TMEM only when the
-//                    row max grows by more than 2^8 (the reference max is otherwise kept,
-//                    which is exact: O and l use the same reference)
-//   O += P.V         tcgen05.mma, A = P (bf16 in smem, K-major over keys), B = V (smem,
-//                    MN-major: head_dim contiguous) -> 128 x 128 fp32 in TMEM [128, 256)
-// K/V pages come by TMA (one 2 KiB box per page and 64-dim half, 128-byte swizzle, no
-// multicast) through a 2-stage ring; Q by two 4-D TMA boxes.  Warp roles: warp 0 TMA
-// producer, warp 1 MMA issuer (one elected thread), warps 4-7 softmax / epilogue.
+// One CTA = a window of 32 consecutive query tokens x one KV head, as two tiles of 16
+// tokens x the KV head's 8 query heads (128 rows = TMEM lanes each).  Both tiles use every
+// K/V block the CTA loads, which halves the shared-memory fill traffic per FLOP against one
+// tile per CTA (the per-SM TMA fill rate, not HBM, bounds a single 128-row tile).  Per key
+// block j of 128 keys and tile t:
+//   S_t  = Q_t.K_j^T  tcgen05.mma kind::f16, A = Q_t (smem, K-major), B = K_j (smem,
+//                     K-major), fp32 128 x 128 in TMEM columns [128 t, 128 t + 128)
+//   softmax           one thread per TMEM lane (= tile row): causal mask from the token's
+//                     position, base-2 online softmax; P (bf16 pairs) is written back over
+//                     the first 64 columns of S_t; O_t is rescaled in TMEM only when the row
+//                     max grows by more than 2^8 (the old reference max is otherwise kept,
+//                     which is exact because O_t and the row sum share the reference)
+//   O_t += P_t.V_j    tcgen05.mma with A = P_t read from TMEM, B = V_j (smem, MN-major),
+//                     fp32 in TMEM columns [256 + 128 t, 384 + 128 t)
+// MMA issue order per block: S_0(j), O_1 += P_1 V(j-1), S_1(j), O_0 += P_0 V(j).  Each
+// softmax thus has two MMAs' time for its block, the two softmax warpgroups run on
+// alternate halves of the period, and the tensor pipe is never left empty.  tcgen05.mma
+// operations of one thread execute in issue order, so S_t(j+1) may be issued right after
+// the P_t.V(j) that reads P_t from the same columns; every other hand-off goes through an
+// mbarrier.  K and V pages come by TMA (one 2 KiB box per page and 64-dim half, 128-byte
+// swizzle, no multicast) through two-stage rings filled by three producer warps, because
+// one thread issues its TMA copies one after another.
+//
+// Warps: 0 producer (Q, K d 0-63), 1 MMA issuer (one elected lane), 2 segment scan then producer
+// (K d 64-127), 3 producer (V), 4-7 softmax / epilogue of tile 0, 8-11 of tile 1 (TMEM lane
+// quadrant = warp % 4).  Registers are moved from the producer warpgroup to the softmax
+// warpgroups with setmaxnreg: 384 threads launch with 168 registers each (64,512) and end
+// with 72 (warps 0-3) + 2 x 216 (warps 4-11) per thread, 64,512 in total.
 #include <cuda_bf16.h>
 #include <math_constants.h>
 
+#include <climits>
 #include <mutex>
 
 #include "attention.cuh"
@@ -30,26 +46,37 @@ namespace ss {
 
 namespace {
 
-constexpr int kTQ = 16;                        // query tokens per tile
+constexpr int kTiles = 2;
+constexpr int kTQT = 16;                       // query tokens per tile
+constexpr int kTQ = kTiles * kTQT;             // query tokens per CTA window
 constexpr int kGroup = 8;                      // query heads per KV head (this kernel)
-constexpr int kRowsT = kTQ * kGroup;           // 128 tile rows (M)
+constexpr int kRowsT = kTQT * kGroup;          // 128 tile rows (M)
 constexpr int kHDp = 128;                      // head dim (K of S, N of O)
 constexpr int kNB = 128;                       // keys per block (N of S, K of O)
 constexpr int kPgPerBlk = kNB / kPage;         // 8 pages per block
-constexpr int kStagesP = 2;
-constexpr int kThreadsP = 256;
+constexpr int kStages = 2;                     // K and V ring depth
+constexpr int kThreadsP = 384;
+constexpr int kLaunchRegs = 168;               // 65,536 / 384, rounded down to 8
+constexpr int kRegsProducer = 72, kRegsSoftmax = 216;
+static_assert(128 * kRegsProducer + 256 * kRegsSoftmax <= kThreadsP * kLaunchRegs,
+              "setmaxnreg split exceeds the launch register pool");
 constexpr int kMinRunP = 2;                    // tokens of runs >= 2 are prefill tokens
-constexpr uint32_t kTmemCols = 256;            // S [0,128) + O [128,256)
+constexpr int kPolyEvery = 4;                  // one exponential pair in 4 on the FMA pipe
+constexpr uint32_t kTmemCols = 512;            // S_0 S_1 [0,256), O_0 O_1 [256,512)
+constexpr uint32_t kColO = 256;
 
 // Shared memory (1024-aligned base).  Every operand tile is [2 halves of 64][rows][128 B].
-constexpr int kQBytes = 2 * kRowsT * 128;      // 32 KiB
-constexpr int kKVBytes = 2 * kNB * 128;        // 32 KiB for K (or V) of one block
+constexpr int kQBytes = 2 * kRowsT * 128;      // 32 KiB per tile
+constexpr int kKVBytes = 2 * kNB * 128;        // 32 KiB: K (or V) of one key block
 constexpr int kOffQ = 0;
-constexpr int kOffK = kOffQ + kQBytes;                       // + s * 2 * kKVBytes
-constexpr int kOffP = kOffK + kStagesP * 2 * kKVBytes;       // 32 KiB
-constexpr int kOffBarP = kOffP + 2 * kRowsT * 128;
-// barriers: q_full, s_full, s_free, p_full, o_done, kv_full[2], kv_empty[2]
-constexpr int kNumBars = 5 + 2 * kStagesP;
+constexpr int kOffK = kOffQ + kTiles * kQBytes;
+constexpr int kOffV = kOffK + kStages * kKVBytes;
+constexpr int kOffBarP = kOffV + kStages * kKVBytes;
+// barriers: q_full, s_full[tile], p_full[tile], pv_done[tile], k_full/k_empty[stage],
+// v_full/v_empty[stage]
+constexpr int kBarQ = 0, kBarS = 1, kBarP = 3, kBarPV = 5, kBarKF = 7;
+constexpr int kBarKE = kBarKF + kStages, kBarVF = kBarKE + kStages, kBarVE = kBarVF + kStages;
+constexpr int kNumBars = kBarVE + kStages;
 constexpr int kOffCtlP = kOffBarP + 8 * kNumBars;
 constexpr int kMaxSeg = kTQ;
 
@@ -63,7 +90,37 @@ struct CtlP {
 };
 constexpr int kSmemP = kOffCtlP + static_cast<int>(sizeof(CtlP)) + 1024;
 
-__device__ __forceinline__ uint32_t bar_addr(uint32_t base, int i) { return base + 8 * i; }
+// 2^x for a pair of fp32 values on the FMA pipe, offloading the MUFU unit (which computes
+// 16 exponentials per clock per SM, as many as the tensor core needs here at full rate).
+// Method: Cody-Waite range reduction 2^x = 2^n * 2^f with n = rint(x) (the 1.5 * 2^23
+// addition trick, round-to-nearest), f in [-1/2, 1/2], and a cubic for 2^f whose
+// coefficients are a minimax fit for relative error made for this kernel by iteratively
+// reweighted least squares (Lawson's algorithm) on 4001 Chebyshev nodes: fit error
+// 7.5e-5, measured 1.3e-4 in fp32 evaluation (bf16 P keeps 2^-9 = 2.0e-3).  Inputs are
+// clamped to >= -126 so 2^n stays a normal power of two; the result for x < -126 is
+// below 1.2e-38 instead of 0, which no sum of P notices.  2^n is applied by adding
+// n << 23 to the exponent field: the low 9 bits of rint's float pattern hold n mod 512.
+__device__ __forceinline__ uint64_t exp2_poly2(uint64_t x2) {
+  float x0, x1;
+  f2unpack(x2, x0, x1);
+  x2 = f2pack(fmaxf(x0, -126.f), fmaxf(x1, -126.f));
+  const uint64_t magic = f2pack(12582912.f, 12582912.f), nmagic = f2pack(-12582912.f, -12582912.f);
+  const uint64_t j2 = add2(x2, magic);
+  const uint64_t r2 = add2(j2, nmagic);                       // rint(x), exact
+  const uint64_t f2 = fma2(r2, f2pack(-1.f, -1.f), x2);       // x - rint(x), exact
+  uint64_t p2 = fma2(f2pack(0x1.c3f76p-5f, 0x1.c3f76p-5f), f2, f2pack(0x1.f0de1cp-3f, 0x1.f0de1cp-3f));
+  p2 = fma2(p2, f2, f2pack(0x1.62f31ap-1f, 0x1.62f31ap-1f));
+  p2 = fma2(p2, f2, f2pack(0x1.fff692p-1f, 0x1.fff692p-1f));
+  float p0, p1, j0, j1;
+  f2unpack(p2, p0, p1);
+  f2unpack(j2, j0, j1);
+  return f2pack(__int_as_float(__float_as_int(p0) + (__float_as_int(j0) << 23)),
+                __int_as_float(__float_as_int(p1) + (__float_as_int(j1) << 23)));
+}
+
+__device__ __forceinline__ int seg_blocks(const CtlP* ctl, int s) {
+  return (ctl->seg_keys[s] + kNB - 1) / kNB;
+}
 
 template <int D>
 __global__ void __launch_bounds__(kThreadsP, 1)
@@ -75,12 +132,9 @@ __global__ void __launch_bounds__(kThreadsP, 1)
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
                                              ~static_cast<uintptr_t>(1023));
   const uint32_t sb = smem_u32(smem);
-  const uint32_t sQ = sb + kOffQ, sK0 = sb + kOffK, sP = sb + kOffP;
+  const uint32_t sQ = sb + kOffQ, sK0 = sb + kOffK, sV0 = sb + kOffV;
   const uint32_t bars = sb + kOffBarP;
-  const uint32_t q_full = bar_addr(bars, 0), s_full = bar_addr(bars, 1), s_free = bar_addr(bars, 2);
-  const uint32_t p_full = bar_addr(bars, 3), o_done = bar_addr(bars, 4);
-  auto kv_full = [&](int s) { return bar_addr(bars, 5 + s); };
-  auto kv_empty = [&](int s) { return bar_addr(bars, 5 + kStagesP + s); };
+  auto bar = [&](int i) { return bars + 8 * i; };
   CtlP* ctl = reinterpret_cast<CtlP*>(smem + kOffCtlP);
 
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
@@ -88,23 +142,26 @@ __global__ void __launch_bounds__(kThreadsP, 1)
   const int kvh = blockIdx.y;
 
   if (tid == 0) {
-    mbar_init(q_full, 1);
-    mbar_init(s_full, 1);
-    mbar_init(s_free, 128);
-    mbar_init(p_full, 128);
-    mbar_init(o_done, 1);
-    for (int s = 0; s < kStagesP; ++s) {
-      mbar_init(kv_full(s), 1);
-      mbar_init(kv_empty(s), 1);
+    mbar_init(bar(kBarQ), 1);
+    for (int t = 0; t < kTiles; ++t) {
+      mbar_init(bar(kBarS + t), 1);
+      mbar_init(bar(kBarP + t), 128);
+      mbar_init(bar(kBarPV + t), 1);
+    }
+    for (int s = 0; s < kStages; ++s) {
+      mbar_init(bar(kBarKF + s), 2);  // two producer warps per K block
+      mbar_init(bar(kBarKE + s), 1);
+      mbar_init(bar(kBarVF + s), 1);
+      mbar_init(bar(kBarVE + s), 1);
     }
     fence_mbar_init();
   }
-  // Segments of this 16-token window: maximal runs of prefill tokens of one sequence.
+  // Segments of this 32-token window: maximal runs of prefill tokens of one sequence.
   if (warp == 2) {
     const long long t = t0 + lane;
     long long seq = -1;
     int pre = 0, pos = 0;
-    if (lane < kTQ && t < a.T) {
+    if (t < a.T) {
       // Same predicate as the decode kernel: every token of a multi-token run is ours.
       const TokInfo ti = token_info(a, t, false);
       seq = ti.seq;
@@ -125,14 +182,11 @@ __global__ void __launch_bounds__(kThreadsP, 1)
       const int ends = (lane == 31) || !((pm >> (lane + 1)) & 1) || next_seq != seq;
       if (ends) ctl->seg_last[idx] = lane;
     }
-    // Keys of a segment = max over its tokens (positions grow inside a chunk, but do not
-    // rely on it): reduce per segment with a simple loop in lane 0.
     __syncwarp();
     const int nseg = __popc(sm);
-    int keys_of_lane = pos;
-    for (int sgi = 0; sgi < nseg; ++sgi) {
+    for (int sgi = 0; sgi < nseg; ++sgi) {  // keys of a segment = max over its rows
       const int f = ctl->seg_first[sgi], l = ctl->seg_last[sgi];
-      int v = (lane >= f && lane <= l) ? keys_of_lane : 0;
+      int v = (lane >= f && lane <= l) ? pos : 0;
 #pragma unroll
       for (int o = 16; o > 0; o >>= 1) v = max(v, __shfl_xor_sync(0xffffffffu, v, o));
       if (lane == 0) ctl->seg_keys[sgi] = v;
@@ -148,236 +202,305 @@ __global__ void __launch_bounds__(kThreadsP, 1)
   tc_fence_after();
   const int nseg = ctl->nseg;
   const uint32_t tmem = ctl->tmem_base;
-  const uint32_t tS = tmem, tO = tmem + kNB;
+  int nblk_total = 0;
+  for (int s = 0; s < nseg; ++s) nblk_total += seg_blocks(ctl, s);
 
-  if (nseg > 0) {
-    if (warp == 0) {
-      // ============================== TMA producer ==============================
-      if (lane == 0) {
+  if (warp < 4) setmaxnreg_dec<kRegsProducer>();  // every warp of warpgroups 0-2 runs one
+  if (warp < 4 && nblk_total > 0 && warp != 1) {
+    // ============================ TMA producers (3 warps) ============================
+    // One thread issues TMA copies one after another, so three warps share each block's
+    // 32 page boxes: warp 0 K d 0-63, warp 2 K d 64-127, warp 3 all of V.
+    const int r = warp == 0 ? 0 : warp - 1;
+    const bool is_v = r == 2;
+    const int ndh = is_v ? 2 : 1, dh0 = is_v ? 0 : r;
+    const CUtensorMap* tm = is_v ? &tmV : &tmK;
+    const uint32_t base0 = is_v ? sV0 : sK0 + dh0 * (kKVBytes / 2);
+    const int full0 = is_v ? kBarVF : kBarKF, empty0 = is_v ? kBarVE : kBarKE;
+    if (lane == 0) {
+      prefetch_tensormap(tm);
+      if (r == 0) {
         prefetch_tensormap(&tmQ);
-        prefetch_tensormap(&tmK);
-        prefetch_tensormap(&tmV);
-        mbar_arrive_expect_tx(q_full, kQBytes);
-        tma_load_4d(sQ, &tmQ, q_full, 0, 0, kvh * kGroup, static_cast<int>(t0));
-        tma_load_4d(sQ + kQBytes / 2, &tmQ, q_full, 0, 1, kvh * kGroup, static_cast<int>(t0));
+        mbar_arrive_expect_tx(bar(kBarQ), kTiles * kQBytes);
+        for (int t = 0; t < kTiles; ++t)
+          for (int dh = 0; dh < 2; ++dh)
+            tma_load_4d(sQ + t * kQBytes + dh * (kQBytes / 2), &tmQ, bar(kBarQ), 0, dh,
+                        kvh * kGroup, static_cast<int>(t0) + t * kTQT);
       }
-      int st = 0;
-      uint32_t ph = 0;
-      bool ok = true;
-      for (int sgi = 0; sgi < nseg && ok; ++sgi) {
-        const long long seq = ctl->seg_seq[sgi];
-        const int keys = ctl->seg_keys[sgi];
-        const int npages = (keys + kPage - 1) / kPage;
-        const int nblk = (keys + kNB - 1) / kNB;
-        for (int j = 0; j < nblk && ok; ++j) {
-          int pg = -1;
-          if (lane < kPgPerBlk) {
-            const int pi = j * kPgPerBlk + lane;
-            if (pi < npages) {
-              const long long pid = ld_index(a.bt, a.bt64, seq * a.bt_sb + pi * a.bt_sn);
-              if (pid < 0 || pid >= a.N) atomicOr(a.err, SS_DEVERR_PAGE);
-              else pg = static_cast<int>(pid);
-            }
-          }
-          int pgs[kPgPerBlk];
-#pragma unroll
-          for (int p = 0; p < kPgPerBlk; ++p) pgs[p] = __shfl_sync(0xffffffffu, pg, p);
-          if (lane == 0) {
-            if (!mbar_wait(kv_empty(st), ph ^ 1)) {
-              ok = false;
-            } else {
-              const uint32_t kdst = sK0 + st * 2 * kKVBytes, vdst = kdst + kKVBytes;
-              mbar_arrive_expect_tx(kv_full(st), 2 * kKVBytes);
-#pragma unroll
-              for (int p = 0; p < kPgPerBlk; ++p) {
-#pragma unroll
-                for (int dh = 0; dh < 2; ++dh) {
-                  const uint32_t off = dh * (kKVBytes / 2) + p * (kPage * 128);
-                  tma_load_5d_nohint(kdst + off, &tmK, kv_full(st), 0, 0, dh, kvh, pgs[p]);
-                  tma_load_5d_nohint(vdst + off, &tmV, kv_full(st), 0, 0, dh, kvh, pgs[p]);
-                }
-              }
-            }
-          }
-          ok = __shfl_sync(0xffffffffu, ok, 0);
-          if (++st == kStagesP) {
-            st = 0;
-            ph ^= 1;
-          }
-        }
+    }
+    // Page ids of block (sgi, j): lanes 0-7, -1 past the segment's pages or out of range.
+    auto page_of = [&](int sgi, int j) -> int {
+      if (sgi >= nseg || lane >= kPgPerBlk) return -1;
+      const int pi = j * kPgPerBlk + lane;
+      if (pi >= (ctl->seg_keys[sgi] + kPage - 1) / kPage) return -1;
+      const long long pid = ld_index(a.bt, a.bt64, ctl->seg_seq[sgi] * a.bt_sb + pi * a.bt_sn);
+      if (pid < 0 || pid >= a.N) {
+        atomicOr(a.err, SS_DEVERR_PAGE);
+        return -1;
       }
-      if (!ok && lane == 0) atomicOr(a.err, SS_DEVERR_TIMEOUT);
-    } else if (warp == 1) {
-      // ============================== MMA issuer ================================
+      return static_cast<int>(pid);
+    };
+    auto advance = [&](int& sgi, int& j) {
+      ++j;
+      while (sgi < nseg && j >= seg_blocks(ctl, sgi)) {
+        ++sgi;
+        j = 0;
+      }
+    };
+    int sgi = 0, j = -1;
+    advance(sgi, j);
+    int pg = page_of(sgi, j);
+    bool ok = true;
+    for (int jg = 0; sgi < nseg && ok; ++jg) {
+      int nsgi = sgi, nj = j;
+      advance(nsgi, nj);
+      const int pg_next = page_of(nsgi, nj);  // block-table load overlaps this block's copies
+      int pgs[kPgPerBlk];
+#pragma unroll
+      for (int p = 0; p < kPgPerBlk; ++p) pgs[p] = __shfl_sync(0xffffffffu, pg, p);
       if (lane == 0) {
-        constexpr uint32_t idesc_qk = idesc_bf16_f32(128, kNB, 0, 0);
-        constexpr uint32_t idesc_pv = idesc_bf16_f32(128, kHDp, 0, 1);
-        int st = 0;
-        uint32_t ph = 0;
-        int jg = 0;
-        bool ok = mbar_wait(q_full, 0);
-        for (int sgi = 0; sgi < nseg && ok; ++sgi) {
-          const int nblk = (ctl->seg_keys[sgi] + kNB - 1) / kNB;
-          for (int j = 0; j < nblk && ok; ++j, ++jg) {
-            const uint32_t kst = sK0 + st * 2 * kKVBytes, vst = kst + kKVBytes;
-            ok = mbar_wait(kv_full(st), ph);
-            if (ok && jg > 0) ok = mbar_wait(s_free, (jg - 1) & 1);
-            if (!ok) break;
-            tc_fence_after();
+        const int st = jg % kStages;
+        ok = mbar_wait(bar(empty0 + st), ((jg / kStages) & 1) ^ 1);
+        if (ok) {
+          const uint32_t dst = base0 + st * kKVBytes;
+          mbar_arrive_expect_tx(bar(full0 + st), ndh * (kKVBytes / 2));
+          for (int h = 0; h < ndh; ++h)
 #pragma unroll
-            for (int kk = 0; kk < kHDp / 16; ++kk) {
-              const uint32_t koff = (kk >> 2) * (kKVBytes / 2) + (kk & 3) * 32;
-              const uint64_t ad = smem_desc_sw128(sQ + (kk >> 2) * (kQBytes / 2) + (kk & 3) * 32, 16, 1024);
-              const uint64_t bd = smem_desc_sw128(kst + koff, 16, 1024);
-              tc_mma_f16(tS, ad, bd, idesc_qk, kk > 0 ? 1u : 0u);
-            }
-            tc_commit(s_full);
-            ok = mbar_wait(p_full, jg & 1);
-            if (!ok) break;
-            tc_fence_after();
-#pragma unroll
-            for (int kk = 0; kk < kNB / 16; ++kk) {
-              const uint64_t ad = smem_desc_sw128(sP + (kk >> 2) * (kRowsT * 128) + (kk & 3) * 32, 16, 1024);
-              const uint64_t bd = smem_desc_sw128(vst + kk * 16 * 128, kKVBytes / 2, 1024);
-              tc_mma_f16(tO, ad, bd, idesc_pv, (j > 0 || kk > 0) ? 1u : 0u);
-            }
-            tc_commit(o_done);
-            tc_commit(kv_empty(st));
-            if (++st == kStagesP) {
-              st = 0;
-              ph ^= 1;
-            }
-          }
+            for (int p = 0; p < kPgPerBlk; ++p)
+              tma_load_5d_nohint(dst + h * (kKVBytes / 2) + p * (kPage * 128), tm, bar(full0 + st),
+                                 0, 0, dh0 + h, kvh, pgs[p]);
         }
-        if (!ok) atomicOr(a.err, SS_DEVERR_TIMEOUT);
+      }
+      ok = __shfl_sync(0xffffffffu, ok, 0);
+      sgi = nsgi;
+      j = nj;
+      pg = pg_next;
+    }
+    if (!ok && lane == 0) atomicOr(a.err, SS_DEVERR_TIMEOUT);
+  } else if (warp < 4 && nblk_total > 0) {
+    // ================================ MMA issuer ==================================
+    // The whole warp walks the schedule and waits; one elected lane issues.  Descriptors
+    // are per-operand bases plus compile-time offsets (the start-address field holds
+    // address / 16 in bits 0-13, and no offset here carries out of it).
+    constexpr uint32_t idesc_qk = idesc_bf16_f32(128, kNB, 0, 0);
+    constexpr uint32_t idesc_pv = idesc_bf16_f32(128, kHDp, 0, 1);
+    const bool leader = elect_one();
+    uint64_t dq[kTiles], dk[kStages], dv[kStages];
+#pragma unroll
+    for (int t = 0; t < kTiles; ++t) dq[t] = smem_desc_sw128(sQ + t * kQBytes, 16, 1024);
+#pragma unroll
+    for (int st = 0; st < kStages; ++st) {
+      dk[st] = smem_desc_sw128(sK0 + st * kKVBytes, 16, 1024);
+      dv[st] = smem_desc_sw128(sV0 + st * kKVBytes, kKVBytes / 2, 1024);
+    }
+    bool ok = mbar_wait(bar(kBarQ), 0);
+    // S_t(jg) = Q_t K(jg)^T into columns [128 t, 128 t + 128).
+    auto issue_qk = [&](int t, int jg) {
+      if (leader) {
+        const uint64_t kd = dk[jg % kStages];
+#pragma unroll
+        for (int kk = 0; kk < kHDp / 16; ++kk) {
+          const uint32_t off = ((kk >> 2) * (kKVBytes / 2) + (kk & 3) * 32) >> 4;
+          const uint32_t qoff = ((kk >> 2) * (kQBytes / 2) + (kk & 3) * 32) >> 4;
+          tc_mma_f16(tmem + t * kNB, dq[t] + qoff, kd + off, idesc_qk, kk > 0 ? 1u : 0u);
+        }
+        tc_commit(bar(kBarS + t));
       }
       __syncwarp();
-    } else if (warp >= 4) {
-      // ========================= softmax + epilogue (1 row per thread) ==========
-      const int wq = warp - 4;            // TMEM lane quadrant of this warp
-      const int row = wq * 32 + lane;     // tile row = token * 8 + head
-      const int rt = row / kGroup, rh = row % kGroup;
-      const long long t = t0 + rt;
-      const uint32_t lane_off = static_cast<uint32_t>(wq * 32) << 16;
-      const float sc = a.scale_log2;
-      int jg = 0;
-      bool ok = true;
-      for (int sgi = 0; sgi < nseg && ok; ++sgi) {
-        const int f = ctl->seg_first[sgi], l = ctl->seg_last[sgi];
-        const bool mine = rt >= f && rt <= l && t < a.T;
-        const int keys = mine ? token_info(a, t, false).L : 0;
-        const int nblk = (ctl->seg_keys[sgi] + kNB - 1) / kNB;
-        if (nblk == 0) {  // no row of the segment has keys: zero output rows
-          if (mine)
-            for (int dd = 0; dd < kHDp; ++dd)
-              a.out[t * a.o_st + static_cast<long long>(kvh * kGroup + rh) * a.o_sh + dd * a.o_sd] =
-                  __float2bfloat16(0.f);
-          continue;
-        }
-        float m_ref = -CUDART_INF_F, lsum = 0.f;
-        for (int j = 0; j < nblk; ++j, ++jg) {
-          ok = mbar_wait(s_full, jg & 1);
-          if (!ok) break;
-          tc_fence_after();
-          uint32_t sr[4][32];
+    };
+    // O_t (+)= P_t(jg) V(jg); P_t sits in the first 64 columns of S_t (16 keys = 8
+    // columns per k-step).
+    auto issue_pv = [&](int t, int jg, bool first_of_seg) -> bool {
+      if (!mbar_wait(bar(kBarP + t), jg & 1)) return false;
+      tc_fence_after();
+      if (leader) {
+        const uint64_t vd = dv[jg % kStages];
 #pragma unroll
-          for (int c = 0; c < 4; ++c) tmem_ld32(tS + lane_off + c * 32, sr[c]);
-          tmem_wait_ld();
-          tc_fence_before();
-          mbar_arrive(s_free);
-          const int kbase = j * kNB;
-          float mblk = -CUDART_INF_F;
+        for (int kk = 0; kk < kNB / 16; ++kk)
+          tc_mma_f16_ts(tmem + kColO + t * kHDp, tmem + t * kNB + kk * 8,
+                        vd + ((kk * 16 * 128) >> 4), idesc_pv,
+                        (!first_of_seg || kk > 0) ? 1u : 0u);
+        tc_commit(bar(kBarPV + t));
+      }
+      __syncwarp();
+      return true;
+    };
+    auto commit = [&](int b) {
+      if (leader) tc_commit(bar(b));
+      __syncwarp();
+    };
+    int jg = 0;
+    bool prev_first = false;
+    for (int sgi = 0; sgi < nseg && ok; ++sgi) {
+      const int nblk = seg_blocks(ctl, sgi);
+      for (int j = 0; j < nblk && ok; ++j, ++jg) {
+        const int st = jg % kStages;
+        ok = mbar_wait(bar(kBarKF + st), (jg / kStages) & 1);
+        if (!ok) break;
+        tc_fence_after();
+        issue_qk(0, jg);
+        if (jg > 0) {
+          ok = issue_pv(1, jg - 1, prev_first);
+          if (!ok) break;
+          commit(kBarVE + (jg - 1) % kStages);  // both tiles have read V(jg - 1)
+        }
+        issue_qk(1, jg);
+        commit(kBarKE + st);                     // both tiles have read K(jg)
+        ok = mbar_wait(bar(kBarVF + st), (jg / kStages) & 1);
+        if (ok) ok = issue_pv(0, jg, j == 0);
+        prev_first = (j == 0);
+      }
+    }
+    if (ok) {
+      ok = issue_pv(1, jg - 1, prev_first);
+      if (ok) commit(kBarVE + (jg - 1) % kStages);
+    }
+    if (!ok && lane == 0) atomicOr(a.err, SS_DEVERR_TIMEOUT);
+  } else if (warp >= 4) {
+    // ============== softmax + epilogue (1 row per thread, one tile per warpgroup) ===========
+    setmaxnreg_inc<kRegsSoftmax>();
+    const int tt = (warp - 4) >> 2;      // tile of this warpgroup
+    const int wq = warp & 3;             // TMEM lane quadrant of this warp
+    const int row = wq * 32 + lane;      // tile row = token * 8 + head
+    const int rt = tt * kTQT + row / kGroup, rh = row % kGroup;  // window token, head
+    const long long t = t0 + rt;
+    const uint32_t lane_off = static_cast<uint32_t>(wq * 32) << 16;
+    const uint32_t tS = tmem + tt * kNB + lane_off, tO = tmem + kColO + tt * kHDp + lane_off;
+    const float sc = a.scale_log2;
+    int jg = 0;
+    bool ok = true;
+    for (int sgi = 0; sgi < nseg && ok; ++sgi) {
+      const int f = ctl->seg_first[sgi], l = ctl->seg_last[sgi];
+      const bool mine = rt >= f && rt <= l && t < a.T;
+      const int keys = mine ? token_info(a, t, false).L : 0;
+      const int nblk = seg_blocks(ctl, sgi);
+      __nv_bfloat16* op = a.out + t * a.o_st + static_cast<long long>(kvh * kGroup + rh) * a.o_sh;
+      if (nblk == 0) {  // no row of the segment has keys: zero output rows
+        if (mine)
+          for (int dd = 0; dd < kHDp; ++dd) op[dd * a.o_sd] = __float2bfloat16(0.f);
+        continue;
+      }
+      // Rows outside the segment compute on whatever their Q row holds and are discarded,
+      // so they are never masked (this keeps full blocks mask-free for the whole warp).
+      const int lim = mine ? keys : INT_MAX;
+      float m_ref = -CUDART_INF_F, lsum = 0.f;
+      for (int j = 0; j < nblk; ++j, ++jg) {
+        ok = mbar_wait(bar(kBarS + tt), jg & 1);
+        if (!ok) break;
+        tc_fence_after();
+        uint32_t sr[4][32];
+#pragma unroll
+        for (int c = 0; c < 4; ++c) tmem_ld32(tS + c * 32, sr[c]);
+        tmem_wait_ld();
+        const int nv = lim - j * kNB;  // valid columns of this row in this block
+        if (!__all_sync(0xffffffffu, nv >= kNB)) {
 #pragma unroll
           for (int c = 0; c < 4; ++c)
 #pragma unroll
-            for (int i = 0; i < 32; ++i) {
-              const float x = (kbase + c * 32 + i < keys) ? __uint_as_float(sr[c][i]) * sc : -CUDART_INF_F;
-              sr[c][i] = __float_as_uint(x);
-              mblk = fmaxf(mblk, x);
-            }
-          // Keep the reference max unless this block raises it by more than 8 (2^8 in p).
-          const bool raise = mblk > m_ref + 8.f;
-          const float m_new = raise ? mblk : m_ref;
-          const float alpha = (raise && m_ref != -CUDART_INF_F) ? ex2(m_ref - m_new) : (raise ? 0.f : 1.f);
-          if (j > 0) {  // PV of the previous block must be done: O stable, P buffer free
-            ok = mbar_wait(o_done, (jg - 1) & 1);
-            if (!ok) break;
-            tc_fence_after();
-            if (__any_sync(0xffffffffu, raise)) {
-#pragma unroll
-              for (int c = 0; c < 4; ++c) {
-                uint32_t orow[32];
-                tmem_ld32(tO + lane_off + c * 32, orow);
-                tmem_wait_ld();
-#pragma unroll
-                for (int i = 0; i < 32; ++i) orow[i] = __float_as_uint(__uint_as_float(orow[i]) * alpha);
-                tmem_st32(tO + lane_off + c * 32, orow);
-              }
-              tmem_wait_st();
-            }
-          }
-          lsum *= alpha;
-          m_ref = m_new;
-          const float ms = m_ref == -CUDART_INF_F ? 0.f : m_ref;
-          // P row -> shared memory, bf16, 128-byte swizzled K-major tile [2][128 rows][128 B].
-#pragma unroll
-          for (int c = 0; c < 4; ++c) {
-#pragma unroll
-            for (int q8 = 0; q8 < 4; ++q8) {
-              float pv[8];
-#pragma unroll
-              for (int e = 0; e < 8; ++e) {
-                pv[e] = ex2(__uint_as_float(sr[c][q8 * 8 + e]) - ms);
-                lsum += pv[e];
-              }
-              const int key = c * 32 + q8 * 8;  // first key of this 16-byte chunk
-              const int kh = key >> 6, chunk = (key & 63) >> 3;
-              const uint32_t addr = sP + kh * (kRowsT * 128) + row * 128 + ((chunk ^ (row & 7)) << 4);
-              asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(addr),
-                           "r"(pack_bf16(pv[0], pv[1])), "r"(pack_bf16(pv[2], pv[3])),
-                           "r"(pack_bf16(pv[4], pv[5])), "r"(pack_bf16(pv[6], pv[7]))
-                           : "memory");
-            }
-          }
-          fence_proxy_async_smem();
-          tc_fence_before();
-          mbar_arrive(p_full);
+            for (int i = 0; i < 32; ++i)
+              if (c * 32 + i >= nv) sr[c][i] = __float_as_uint(-CUDART_INF_F);
         }
-        if (!ok) break;
-        // ---- epilogue: O / l -> bf16 ---------------------------------------------------
-        ok = mbar_wait(o_done, (jg - 1) & 1);
-        if (!ok) break;
-        tc_fence_after();
-        const float inv = lsum > 0.f ? 1.f / lsum : 0.f;
-        __nv_bfloat16* op = a.out + t * a.o_st + static_cast<long long>(kvh * kGroup + rh) * a.o_sh;
-        const bool vec = mine && a.o_sd == 1 && ((reinterpret_cast<uintptr_t>(op) & 15) == 0);
+        // Row max of the raw scores: four independent chains of three-input maxima.
+        float mc[4];
 #pragma unroll
         for (int c = 0; c < 4; ++c) {
-          uint32_t orow[32];
-          tmem_ld32(tO + lane_off + c * 32, orow);
-          tmem_wait_ld();
-          if (mine) {
-            if (vec) {
+          float m = fmaxf(__uint_as_float(sr[c][0]), __uint_as_float(sr[c][1]));
 #pragma unroll
-              for (int q8 = 0; q8 < 4; ++q8) {
-                uint4 v;
-                v.x = pack_bf16(__uint_as_float(orow[q8 * 8 + 0]) * inv, __uint_as_float(orow[q8 * 8 + 1]) * inv);
-                v.y = pack_bf16(__uint_as_float(orow[q8 * 8 + 2]) * inv, __uint_as_float(orow[q8 * 8 + 3]) * inv);
-                v.z = pack_bf16(__uint_as_float(orow[q8 * 8 + 4]) * inv, __uint_as_float(orow[q8 * 8 + 5]) * inv);
-                v.w = pack_bf16(__uint_as_float(orow[q8 * 8 + 6]) * inv, __uint_as_float(orow[q8 * 8 + 7]) * inv);
-                *reinterpret_cast<uint4*>(op + c * 32 + q8 * 8) = v;
-              }
-            } else {
+          for (int i = 2; i < 32; i += 2)
+            m = max3(m, __uint_as_float(sr[c][i]), __uint_as_float(sr[c][i + 1]));
+          mc[c] = m;
+        }
+        const float mblk = max3(mc[0], mc[1], fmaxf(mc[2], mc[3])) * sc;  // sc > 0
+        // Keep the reference max unless this block raises it by more than 8 (2^8 in p).
+        const bool raise = mblk > m_ref + 8.f;
+        const float m_new = raise ? mblk : m_ref;
+        const float alpha = raise ? (m_ref == -CUDART_INF_F ? 0.f : ex2(m_ref - m_new)) : 1.f;
+        if (j > 0 && __any_sync(0xffffffffu, raise)) {
+          // Rescale O_t in place.  S_t(jg) completing implies P_t.V(jg - 1) completed (the
+          // MMA thread issued it earlier); the wait below returns at once.
+          ok = mbar_wait(bar(kBarPV + tt), (jg - 1) & 1);
+          if (!ok) break;
+          tc_fence_after();
 #pragma unroll
-              for (int i = 0; i < 32; ++i)
-                op[static_cast<long long>(c * 32 + i) * a.o_sd] = __float2bfloat16(__uint_as_float(orow[i]) * inv);
-            }
+          for (int c = 0; c < 4; ++c) {
+            uint32_t orow[32];
+            tmem_ld32(tO + c * 32, orow);
+            tmem_wait_ld();
+#pragma unroll
+            for (int i = 0; i < 32; ++i) orow[i] = __float_as_uint(__uint_as_float(orow[i]) * alpha);
+            tmem_st32(tO + c * 32, orow);
           }
         }
-        tc_fence_before();  // O reads complete before the next segment's P.V overwrites O
+        m_ref = m_new;
+        const float ms = m_ref == -CUDART_INF_F ? 0.f : m_ref;
+        const uint64_t sc2 = f2pack(sc, sc), nms2 = f2pack(-ms, -ms);
+        uint64_t acc[4] = {0, 0, 0, 0};  // four independent packed partial row sums
+        // p = 2^(s sc - m): paired fma, then the hardware exponential for most pairs and the
+        // polynomial on the FMA pipe for one pair in kPolyEvery; P as bf16 pairs over the
+        // first 64 columns of S_t (column c holds keys 2c, 2c + 1).
+#pragma unroll
+        for (int h2 = 0; h2 < 2; ++h2) {
+          uint32_t pk[32];
+#pragma unroll
+          for (int i = 0; i < 32; ++i) {
+            const int k0 = h2 * 64 + 2 * i;
+            const uint64_t x2 = fma2(f2pack(__uint_as_float(sr[k0 >> 5][k0 & 31]),
+                                            __uint_as_float(sr[(k0 + 1) >> 5][(k0 + 1) & 31])),
+                                     sc2, nms2);
+            uint64_t p2;
+            if ((i % kPolyEvery) == kPolyEvery - 1) {
+              p2 = exp2_poly2(x2);
+            } else {
+              float x0, x1;
+              f2unpack(x2, x0, x1);
+              p2 = f2pack(ex2(x0), ex2(x1));
+            }
+            acc[i & 3] = add2(acc[i & 3], p2);
+            float p0, p1;
+            f2unpack(p2, p0, p1);
+            pk[i] = pack_bf16(p0, p1);
+          }
+          tmem_st32(tS + h2 * 32, pk);
+        }
+        tmem_wait_st();
+        tc_fence_before();
+        mbar_arrive(bar(kBarP + tt));
+        float s0, s1;
+        f2unpack(add2(add2(acc[0], acc[1]), add2(acc[2], acc[3])), s0, s1);
+        lsum = lsum * alpha + (s0 + s1);
       }
-      if (!ok && lane == 0) atomicOr(a.err, SS_DEVERR_TIMEOUT);
+      if (!ok) break;
+      // ---- epilogue: O_t / l -> bf16 ---------------------------------------------------
+      ok = mbar_wait(bar(kBarPV + tt), (jg - 1) & 1);
+      if (!ok) break;
+      tc_fence_after();
+      const float inv = lsum > 0.f ? 1.f / lsum : 0.f;
+      const bool vec = mine && a.o_sd == 1 && ((reinterpret_cast<uintptr_t>(op) & 15) == 0);
+#pragma unroll
+      for (int c = 0; c < 4; ++c) {
+        uint32_t orow[32];
+        tmem_ld32(tO + c * 32, orow);
+        tmem_wait_ld();
+        if (mine) {
+          if (vec) {
+#pragma unroll
+            for (int q8 = 0; q8 < 4; ++q8) {
+              uint4 v;
+              v.x = pack_bf16(__uint_as_float(orow[q8 * 8 + 0]) * inv, __uint_as_float(orow[q8 * 8 + 1]) * inv);
+              v.y = pack_bf16(__uint_as_float(orow[q8 * 8 + 2]) * inv, __uint_as_float(orow[q8 * 8 + 3]) * inv);
+              v.z = pack_bf16(__uint_as_float(orow[q8 * 8 + 4]) * inv, __uint_as_float(orow[q8 * 8 + 5]) * inv);
+              v.w = pack_bf16(__uint_as_float(orow[q8 * 8 + 6]) * inv, __uint_as_float(orow[q8 * 8 + 7]) * inv);
+              *reinterpret_cast<uint4*>(op + c * 32 + q8 * 8) = v;
+            }
+          } else {
+#pragma unroll
+            for (int i = 0; i < 32; ++i)
+              op[static_cast<long long>(c * 32 + i) * a.o_sd] = __float2bfloat16(__uint_as_float(orow[i]) * inv);
+          }
+        }
+      }
+      tc_fence_before();  // O_t reads complete before the next segment's P.V overwrites O_t
     }
+    if (!ok && lane == 0) atomicOr(a.err, SS_DEVERR_TIMEOUT);
   }
   // ---- teardown ------------------------------------------------------------------------
   tc_fence_before();
@@ -391,11 +514,25 @@ __global__ void __launch_bounds__(kThreadsP, 1)
   griddep_wait();
 }
 
+// The setmaxnreg split needs the kernel to launch with kLaunchRegs registers per thread.
+bool launch_regs_ok() {
+  static std::once_flag once;
+  static bool ok = false;
+  std::call_once(once, [] {
+    cudaFuncAttributes fa;
+    ok = cudaFuncGetAttributes(&fa, prefill_attention_kernel<kHDp>) == cudaSuccess &&
+         fa.numRegs == kLaunchRegs;
+  });
+  return ok;
+}
+
 }  // namespace
 
 bool prefill_supported(const AttnArgs& a) {
+  // scale_log2 > 0: the row max is taken over the unscaled scores.
   return a.D == kHDp && a.group == kGroup && a.q_sd == 1 && (a.q_sh % 8) == 0 &&
-         (a.q_st % 8) == 0 && (reinterpret_cast<uintptr_t>(a.q) & 15) == 0;
+         (a.q_st % 8) == 0 && (reinterpret_cast<uintptr_t>(a.q) & 15) == 0 &&
+         a.scale_log2 > 0.f && launch_regs_ok();
 }
 
 int prefill_min_run() { return kMinRunP; }
