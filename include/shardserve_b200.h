@@ -86,10 +86,12 @@ SS_API int ss_kv_append(const void* k, const int64_t k_strides[3], const void* v
 
 /*
  * Workspace size (bytes) that ss_ragged_paged_attention needs on `device` for this geometry.
- * Byte 0..3 of the workspace is the device error word (zero it to start clean); the rest is
- * scratch that every call rewrites before reading (split-K partial states and per-row split
- * descriptors), so one buffer can be reused across calls on one stream without clearing.
- * Calls that run concurrently on different streams need different workspaces.
+ * Byte 0..3 of the workspace is the device error word (zero it to start clean).  Bytes
+ * 64..71 hold the chunked-prefill work counter: they must be zero before the first call (a
+ * freshly zeroed buffer) and every call leaves them zero.  The rest is scratch that every
+ * call rewrites before reading (split-K partial states and per-row split descriptors), so
+ * one buffer can be reused across calls on one stream without clearing.  Calls that run
+ * concurrently on different streams need different workspaces.
  */
 SS_API int ss_attention_workspace_bytes(int device, int64_t tokens, int heads, int kv_heads,
                                  int head_dim, size_t* bytes);

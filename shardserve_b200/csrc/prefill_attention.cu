@@ -28,6 +28,13 @@
 // swizzle, no multicast) through two-stage rings filled by three producer warps, because
 // one thread issues its TMA copies one after another.
 //
+// Scheduling: the grid is persistent (one CTA per SM, at most one per work item).  A work
+// item is (32-token window, KV head); every CTA ranks the windows by an estimate of the key
+// blocks their segments walk and takes items longest first from an atomic counter in the
+// workspace header, so the wave tail is made of the shortest items.  The last CTA to
+// finish returns the counter to zero for the next launch.  P.V of keys 0-63 starts once
+// that half of P is written.
+//
 // Warps: 0 producer (Q, K d 0-63), 1 MMA issuer (one elected lane), 2 segment scan then producer
 // (K d 64-127), 3 producer (V), 4-7 softmax / epilogue of tile 0, 8-11 of tile 1 (TMEM lane
 // quadrant = warp % 4).  Registers are moved from the producer warpgroup to the softmax
@@ -36,6 +43,7 @@
 #include <cuda_bf16.h>
 #include <math_constants.h>
 
+#include <algorithm>
 #include <climits>
 #include <mutex>
 
@@ -72,23 +80,28 @@ constexpr int kOffQ = 0;
 constexpr int kOffK = kOffQ + kTiles * kQBytes;
 constexpr int kOffV = kOffK + kStages * kKVBytes;
 constexpr int kOffBarP = kOffV + kStages * kKVBytes;
-// barriers: q_full, s_full[tile], p_full[tile], pv_done[tile], k_full/k_empty[stage],
-// v_full/v_empty[stage]
-constexpr int kBarQ = 0, kBarS = 1, kBarP = 3, kBarPV = 5, kBarKF = 7;
+// barriers: q_full, s_full[tile], p_full[tile], pv_done[tile], p_half[tile] (P of keys
+// 0-63 written), k_full/k_empty[stage], v_full/v_empty[stage]
+constexpr int kBarQ = 0, kBarS = 1, kBarP = 3, kBarPV = 5, kBarPH = 7, kBarKF = 9;
 constexpr int kBarKE = kBarKF + kStages, kBarVF = kBarKE + kStages, kBarVE = kBarVF + kStages;
 constexpr int kNumBars = kBarVE + kStages;
 constexpr int kOffCtlP = kOffBarP + 8 * kNumBars;
 constexpr int kMaxSeg = kTQ;
+constexpr int kMaxWinSort = 1024;              // windows ranked longest first (else in order)
+constexpr int kSchedWord = 16;                 // workspace header words: next item, CTAs done
 
 struct CtlP {
   uint32_t tmem_base;
+  int item[2];             // work item of even / odd iterations (from the atomic counter)
+  int abort;               // set when a bounded wait timed out: stop after this item
   int nseg;
   int seg_first[kMaxSeg];  // window-relative first token of each segment
   int seg_last[kMaxSeg];
   long long seg_seq[kMaxSeg];
   int seg_keys[kMaxSeg];   // keys the segment's last row attends (max position + 1, clamped)
 };
-constexpr int kSmemP = kOffCtlP + static_cast<int>(sizeof(CtlP)) + 1024;
+constexpr int kOffSort = (kOffCtlP + static_cast<int>(sizeof(CtlP)) + 15) / 16 * 16;
+constexpr int kSmemP = kOffSort + 2 * 4 * kMaxWinSort + 1024;  // + window cost and order
 
 // 2^x for a pair of fp32 values on the FMA pipe, offloading the MUFU unit (which computes
 // 16 exponentials per clock per SM, as many as the tensor core needs here at full rate).
@@ -118,6 +131,12 @@ __device__ __forceinline__ uint64_t exp2_poly2(uint64_t x2) {
                 __int_as_float(__float_as_int(p1) + (__float_as_int(j1) << 23)));
 }
 
+// Bounded wait whose outcome every lane of the warp shares (a lane that timed out makes
+// the whole warp leave together, so no later warp-wide operation waits on a missing lane).
+__device__ __forceinline__ bool wait_warp(uint32_t bar, uint32_t parity) {
+  return __all_sync(0xffffffffu, mbar_wait(bar, parity));
+}
+
 __device__ __forceinline__ int seg_blocks(const CtlP* ctl, int s) {
   return (ctl->seg_keys[s] + kNB - 1) / kNB;
 }
@@ -138,8 +157,12 @@ __global__ void __launch_bounds__(kThreadsP, 1)
   CtlP* ctl = reinterpret_cast<CtlP*>(smem + kOffCtlP);
 
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-  const long long t0 = static_cast<long long>(blockIdx.x) * kTQ;
-  const int kvh = blockIdx.y;
+  int* wcost = reinterpret_cast<int*>(smem + kOffSort);
+  int* worder = wcost + kMaxWinSort;
+  unsigned* sched = a.err + kSchedWord;
+  const int nwin = static_cast<int>((a.T + kTQ - 1) / kTQ);
+  const int nitems = nwin * a.KVH;
+  const bool ranked = nwin <= kMaxWinSort;
 
   if (tid == 0) {
     mbar_init(bar(kBarQ), 1);
@@ -147,6 +170,7 @@ __global__ void __launch_bounds__(kThreadsP, 1)
       mbar_init(bar(kBarS + t), 1);
       mbar_init(bar(kBarP + t), 128);
       mbar_init(bar(kBarPV + t), 1);
+      mbar_init(bar(kBarPH + t), 128);
     }
     for (int s = 0; s < kStages; ++s) {
       mbar_init(bar(kBarKF + s), 2);  // two producer warps per K block
@@ -155,363 +179,475 @@ __global__ void __launch_bounds__(kThreadsP, 1)
       mbar_init(bar(kBarVE + s), 1);
     }
     fence_mbar_init();
-  }
-  // Segments of this 32-token window: maximal runs of prefill tokens of one sequence.
-  if (warp == 2) {
-    const long long t = t0 + lane;
-    long long seq = -1;
-    int pre = 0, pos = 0;
-    if (t < a.T) {
-      // Same predicate as the decode kernel: every token of a multi-token run is ours.
-      const TokInfo ti = token_info(a, t, false);
-      seq = ti.seq;
-      pre = token_in_long_run(a, kMinRunP, t, ti.seq) ? 1 : 0;
-      pos = ti.L;  // keys of this row (0 for invalid metadata: the row is written as zeros)
-    }
-    const unsigned pm = __ballot_sync(0xffffffffu, pre);
-    const long long prev_seq = __shfl_up_sync(0xffffffffu, seq, 1);
-    const long long next_seq = __shfl_down_sync(0xffffffffu, seq, 1);
-    const int starts = pre && (lane == 0 || !((pm >> (lane - 1)) & 1) || prev_seq != seq);
-    const unsigned sm = __ballot_sync(0xffffffffu, starts);
-    if (pre) {
-      const int idx = __popc(sm & ((2u << lane) - 1)) - 1;  // segment of this token
-      if (starts) {
-        ctl->seg_first[idx] = lane;
-        ctl->seg_seq[idx] = seq;
-      }
-      const int ends = (lane == 31) || !((pm >> (lane + 1)) & 1) || next_seq != seq;
-      if (ends) ctl->seg_last[idx] = lane;
-    }
-    __syncwarp();
-    const int nseg = __popc(sm);
-    for (int sgi = 0; sgi < nseg; ++sgi) {  // keys of a segment = max over its rows
-      const int f = ctl->seg_first[sgi], l = ctl->seg_last[sgi];
-      int v = (lane >= f && lane <= l) ? pos : 0;
-#pragma unroll
-      for (int o = 16; o > 0; o >>= 1) v = max(v, __shfl_xor_sync(0xffffffffu, v, o));
-      if (lane == 0) ctl->seg_keys[sgi] = v;
-    }
-    if (lane == 0) ctl->nseg = nseg;
+    ctl->abort = 0;
   }
   if (warp == 0) {
     tmem_alloc(smem_u32(&ctl->tmem_base), kTmemCols);
     tmem_relinquish();
   }
+  // Longest first: a window's cost estimates the key blocks its segments walk from its
+  // first and last tokens only (eight independent loads): the last token's segment walks
+  // ceil(keys / 128) blocks, and a different first segment at most ceil((pos + 32) / 128).
+  // Windows are ranked by cost, ties by window index, so every CTA builds the same order.
+  if (ranked) {
+    auto seq_at = [&](long long t) {
+      return t >= 0 && t < a.T ? ld_index(a.seq, a.seq64, t) : -2 - t;  // matches no row
+    };
+    auto blocks_of = [&](long long keys) {
+      return static_cast<int>((min(max(keys, 0ll), a.W * kPage) + kNB - 1) / kNB);
+    };
+    for (int w = tid; w < nwin; w += kThreadsP) {
+      const long long ts = static_cast<long long>(w) * kTQ, te = min(ts + kTQ - 1, a.T - 1);
+      const long long s0 = seq_at(ts - 1), s1 = seq_at(ts), s2 = seq_at(ts + 1);
+      const long long e0 = seq_at(te - 1), e1 = seq_at(te), e2 = seq_at(te + 1);
+      const long long ps = ld_index(a.pos, a.pos64, ts), pe = ld_index(a.pos, a.pos64, te);
+      int c = 0;
+      if (e1 == e0 || e1 == e2) c += blocks_of(pe + 1);                  // last segment
+      if (s1 != e1 && (s1 == s0 || s1 == s2)) c += blocks_of(ps + kTQ);  // first segment
+      wcost[w] = c;
+    }
+    __syncthreads();
+    for (int w = tid; w < nwin; w += kThreadsP) {
+      const int c = wcost[w];
+      int rank = 0;
+      for (int v = 0; v < nwin; ++v) {
+        const int cv = wcost[v];
+        rank += (cv > c) || (cv == c && v < w);
+      }
+      worder[rank] = w;
+    }
+  }
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
-  const int nseg = ctl->nseg;
   const uint32_t tmem = ctl->tmem_base;
-  int nblk_total = 0;
-  for (int s = 0; s < nseg; ++s) nblk_total += seg_blocks(ctl, s);
 
-  if (warp < 4) setmaxnreg_dec<kRegsProducer>();  // every warp of warpgroups 0-2 runs one
-  if (warp < 4 && nblk_total > 0 && warp != 1) {
-    // ============================ TMA producers (3 warps) ============================
-    // One thread issues TMA copies one after another, so three warps share each block's
-    // 32 page boxes: warp 0 K d 0-63, warp 2 K d 64-127, warp 3 all of V.
-    const int r = warp == 0 ? 0 : warp - 1;
-    const bool is_v = r == 2;
-    const int ndh = is_v ? 2 : 1, dh0 = is_v ? 0 : r;
-    const CUtensorMap* tm = is_v ? &tmV : &tmK;
-    const uint32_t base0 = is_v ? sV0 : sK0 + dh0 * (kKVBytes / 2);
-    const int full0 = is_v ? kBarVF : kBarKF, empty0 = is_v ? kBarVE : kBarKE;
-    if (lane == 0) {
-      prefetch_tensormap(tm);
-      if (r == 0) {
-        prefetch_tensormap(&tmQ);
-        mbar_arrive_expect_tx(bar(kBarQ), kTiles * kQBytes);
-        for (int t = 0; t < kTiles; ++t)
-          for (int dh = 0; dh < 2; ++dh)
-            tma_load_4d(sQ + t * kQBytes + dh * (kQBytes / 2), &tmQ, bar(kBarQ), 0, dh,
-                        kvh * kGroup, static_cast<int>(t0) + t * kTQT);
+  // Per-role running counters: block barriers keep their phases across work items.
+  int jg = 0;      // key blocks processed so far by this CTA
+  int qn = 0;      // Q tiles loaded so far (q_full phases)
+  bool ok = true;
+  struct ItemInfo {
+    bool live;
+    long long t0;
+    int kvh, nseg, nblk_total;
+  };
+  // Takes the next work item and scans its window's segments (warp 2).  The item slot
+  // alternates between iterations: thread 0 may write the next item before a thread that
+  // has passed the barrier has read this one.  Nothing else is written between the two
+  // barriers, so every thread takes the same decisions.
+  int iter = 0;
+  auto item_head = [&]() -> ItemInfo {
+    if (tid == 0) ctl->item[iter & 1] = static_cast<int>(atomicAdd(sched, 1u));
+    named_bar_sync(1, kThreadsP);
+    const int item = ctl->item[iter & 1];
+    ++iter;
+    if (item >= nitems || ctl->abort) return ItemInfo{false, 0, 0, 0, 0};
+    const int wi = item / a.KVH;
+    const long long t0 = static_cast<long long>(ranked ? worder[wi] : wi) * kTQ;
+    const int kvh = item % a.KVH;
+    // Segments of this 32-token window: maximal runs of prefill tokens of one sequence.
+    if (warp == 2) {
+      const long long t = t0 + lane;
+      long long seq = -1;
+      int pre = 0, pos = 0;
+      if (t < a.T) {
+        // Same predicate as the decode kernel: every token of a multi-token run is ours.
+        const TokInfo ti = token_info(a, t, false);
+        seq = ti.seq;
+        pre = token_in_long_run(a, kMinRunP, t, ti.seq) ? 1 : 0;
+        pos = ti.L;  // keys of this row (0 for invalid metadata: the row is written as zeros)
       }
-    }
-    // Page ids of block (sgi, j): lanes 0-7, -1 past the segment's pages or out of range.
-    auto page_of = [&](int sgi, int j) -> int {
-      if (sgi >= nseg || lane >= kPgPerBlk) return -1;
-      const int pi = j * kPgPerBlk + lane;
-      if (pi >= (ctl->seg_keys[sgi] + kPage - 1) / kPage) return -1;
-      const long long pid = ld_index(a.bt, a.bt64, ctl->seg_seq[sgi] * a.bt_sb + pi * a.bt_sn);
-      if (pid < 0 || pid >= a.N) {
-        atomicOr(a.err, SS_DEVERR_PAGE);
-        return -1;
+      const unsigned pm = __ballot_sync(0xffffffffu, pre);
+      const long long prev_seq = __shfl_up_sync(0xffffffffu, seq, 1);
+      const long long next_seq = __shfl_down_sync(0xffffffffu, seq, 1);
+      const int starts = pre && (lane == 0 || !((pm >> (lane - 1)) & 1) || prev_seq != seq);
+      const unsigned sm = __ballot_sync(0xffffffffu, starts);
+      if (pre) {
+        const int idx = __popc(sm & ((2u << lane) - 1)) - 1;  // segment of this token
+        if (starts) {
+          ctl->seg_first[idx] = lane;
+          ctl->seg_seq[idx] = seq;
+        }
+        const int ends = (lane == 31) || !((pm >> (lane + 1)) & 1) || next_seq != seq;
+        if (ends) ctl->seg_last[idx] = lane;
       }
-      return static_cast<int>(pid);
-    };
-    auto advance = [&](int& sgi, int& j) {
-      ++j;
-      while (sgi < nseg && j >= seg_blocks(ctl, sgi)) {
-        ++sgi;
-        j = 0;
-      }
-    };
-    int sgi = 0, j = -1;
-    advance(sgi, j);
-    int pg = page_of(sgi, j);
-    bool ok = true;
-    for (int jg = 0; sgi < nseg && ok; ++jg) {
-      int nsgi = sgi, nj = j;
-      advance(nsgi, nj);
-      const int pg_next = page_of(nsgi, nj);  // block-table load overlaps this block's copies
-      int pgs[kPgPerBlk];
+      __syncwarp();
+      const int nseg = __popc(sm);
+      for (int sgi = 0; sgi < nseg; ++sgi) {  // keys of a segment = max over its rows
+        const int f = ctl->seg_first[sgi], l = ctl->seg_last[sgi];
+        int v = (lane >= f && lane <= l) ? pos : 0;
 #pragma unroll
-      for (int p = 0; p < kPgPerBlk; ++p) pgs[p] = __shfl_sync(0xffffffffu, pg, p);
-      if (lane == 0) {
-        const int st = jg % kStages;
-        ok = mbar_wait(bar(empty0 + st), ((jg / kStages) & 1) ^ 1);
+        for (int o = 16; o > 0; o >>= 1) v = max(v, __shfl_xor_sync(0xffffffffu, v, o));
+        if (lane == 0) ctl->seg_keys[sgi] = v;
+      }
+      if (lane == 0) ctl->nseg = nseg;
+    }
+    named_bar_sync(1, kThreadsP);
+    const int nseg = ctl->nseg;
+    int nblk_total = 0;
+    for (int s = 0; s < nseg; ++s) nblk_total += seg_blocks(ctl, s);
+    return ItemInfo{true, t0, kvh, nseg, nblk_total};
+  };
+
+  // The work-item loop is written once per register class so that each keeps its
+  // setmaxnreg budget; both pass named barrier 1 the same number of times.
+  if (warp < 4) {
+    setmaxnreg_dec<kRegsProducer>();
+    for (;;) {
+      const ItemInfo it = item_head();
+      if (!it.live) break;
+      const long long t0 = it.t0;
+      const int kvh = it.kvh, nseg = it.nseg, nblk_total = it.nblk_total;
+      if (nblk_total > 0 && warp != 1) {
+        // ============================ TMA producers (3 warps) ============================
+        // One thread issues TMA copies one after another, so three warps share each block's
+        // 32 page boxes: warp 0 K d 0-63, warp 2 K d 64-127, warp 3 all of V.
+        const int r = warp == 0 ? 0 : warp - 1;
+        const bool is_v = r == 2;
+        const int ndh = is_v ? 2 : 1, dh0 = is_v ? 0 : r;
+        const CUtensorMap* tm = is_v ? &tmV : &tmK;
+        const uint32_t base0 = is_v ? sV0 : sK0 + dh0 * (kKVBytes / 2);
+        const int full0 = is_v ? kBarVF : kBarKF, empty0 = is_v ? kBarVE : kBarKE;
+        if (lane == 0) {
+          prefetch_tensormap(tm);
+          if (r == 0) {
+            prefetch_tensormap(&tmQ);
+            mbar_arrive_expect_tx(bar(kBarQ), kTiles * kQBytes);  // Q is free: the last item's
+                                                                   // MMAs completed before its end
+            for (int t = 0; t < kTiles; ++t)
+              for (int dh = 0; dh < 2; ++dh)
+                tma_load_4d(sQ + t * kQBytes + dh * (kQBytes / 2), &tmQ, bar(kBarQ), 0, dh,
+                            kvh * kGroup, static_cast<int>(t0) + t * kTQT);
+          }
+        }
+        // Page ids of block (sgi, j): lanes 0-7, -1 past the segment's pages or out of range.
+        auto page_of = [&](int sgi, int j) -> int {
+          if (sgi >= nseg || lane >= kPgPerBlk) return -1;
+          const int pi = j * kPgPerBlk + lane;
+          if (pi >= (ctl->seg_keys[sgi] + kPage - 1) / kPage) return -1;
+          const long long pid = ld_index(a.bt, a.bt64, ctl->seg_seq[sgi] * a.bt_sb + pi * a.bt_sn);
+          if (pid < 0 || pid >= a.N) {
+            atomicOr(a.err, SS_DEVERR_PAGE);
+            return -1;
+          }
+          return static_cast<int>(pid);
+        };
+        auto advance = [&](int& sgi, int& j) {
+          ++j;
+          while (sgi < nseg && j >= seg_blocks(ctl, sgi)) {
+            ++sgi;
+            j = 0;
+          }
+        };
+        int sgi = 0, j = -1;
+        advance(sgi, j);
+        int pg = page_of(sgi, j);
+        for (; sgi < nseg && ok; ++jg) {
+          int nsgi = sgi, nj = j;
+          advance(nsgi, nj);
+          const int pg_next = page_of(nsgi, nj);  // block-table load overlaps this block's copies
+          int pgs[kPgPerBlk];
+#pragma unroll
+          for (int p = 0; p < kPgPerBlk; ++p) pgs[p] = __shfl_sync(0xffffffffu, pg, p);
+          if (lane == 0) {
+            const int st = jg % kStages;
+            ok = mbar_wait(bar(empty0 + st), ((jg / kStages) & 1) ^ 1);
+            if (ok) {
+              const uint32_t dst = base0 + st * kKVBytes;
+              mbar_arrive_expect_tx(bar(full0 + st), ndh * (kKVBytes / 2));
+              for (int h = 0; h < ndh; ++h)
+#pragma unroll
+                for (int p = 0; p < kPgPerBlk; ++p)
+                  tma_load_5d_nohint(dst + h * (kKVBytes / 2) + p * (kPage * 128), tm, bar(full0 + st),
+                                     0, 0, dh0 + h, kvh, pgs[p]);
+            }
+          }
+          ok = __shfl_sync(0xffffffffu, ok, 0);
+          sgi = nsgi;
+          j = nj;
+          pg = pg_next;
+        }
+        if (!ok && lane == 0) {
+          atomicOr(a.err, SS_DEVERR_TIMEOUT);
+          ctl->abort = 1;
+        }
+      } else if (nblk_total > 0) {
+        // ================================ MMA issuer ==================================
+        // The whole warp walks the schedule and waits; one elected lane issues.  Descriptors
+        // are per-operand bases plus compile-time offsets (the start-address field holds
+        // address / 16 in bits 0-13, and no offset here carries out of it).
+        constexpr uint32_t idesc_qk = idesc_bf16_f32(128, kNB, 0, 0);
+        constexpr uint32_t idesc_pv = idesc_bf16_f32(128, kHDp, 0, 1);
+        const bool leader = elect_one();
+        uint64_t dq[kTiles], dk[kStages], dv[kStages];
+#pragma unroll
+        for (int t = 0; t < kTiles; ++t) dq[t] = smem_desc_sw128(sQ + t * kQBytes, 16, 1024);
+#pragma unroll
+        for (int st = 0; st < kStages; ++st) {
+          dk[st] = smem_desc_sw128(sK0 + st * kKVBytes, 16, 1024);
+          dv[st] = smem_desc_sw128(sV0 + st * kKVBytes, kKVBytes / 2, 1024);
+        }
+        ok = wait_warp(bar(kBarQ), qn & 1);
+        ++qn;
+        // S_t(jg) = Q_t K(jg)^T into columns [128 t, 128 t + 128).
+        auto issue_qk = [&](int t, int jg) {
+          if (leader) {
+            const uint64_t kd = dk[jg % kStages];
+#pragma unroll
+            for (int kk = 0; kk < kHDp / 16; ++kk) {
+              const uint32_t off = ((kk >> 2) * (kKVBytes / 2) + (kk & 3) * 32) >> 4;
+              const uint32_t qoff = ((kk >> 2) * (kQBytes / 2) + (kk & 3) * 32) >> 4;
+              tc_mma_f16(tmem + t * kNB, dq[t] + qoff, kd + off, idesc_qk, kk > 0 ? 1u : 0u);
+            }
+            tc_commit(bar(kBarS + t));
+          }
+          __syncwarp();
+        };
+        // O_t (+)= P_t(jg) V(jg); P_t sits in the first 64 columns of S_t (16 keys = 8
+        // columns per k-step).
+        // The first four k-steps (keys 0-63) start as soon as that half of P is written.
+        auto issue_pv = [&](int t, int jg, bool first_of_seg) -> bool {
+          const uint64_t vd = dv[jg % kStages];
+#pragma unroll
+          for (int half = 0; half < 2; ++half) {
+            if (!wait_warp(bar((half ? kBarP : kBarPH) + t), jg & 1)) return false;
+            tc_fence_after();
+            if (leader) {
+#pragma unroll
+              for (int kk = half * 4; kk < half * 4 + 4; ++kk)
+                tc_mma_f16_ts(tmem + kColO + t * kHDp, tmem + t * kNB + kk * 8,
+                              vd + ((kk * 16 * 128) >> 4), idesc_pv,
+                              (!first_of_seg || kk > 0) ? 1u : 0u);
+            }
+            __syncwarp();
+          }
+          if (leader) tc_commit(bar(kBarPV + t));
+          __syncwarp();
+          return true;
+        };
+        auto commit = [&](int b) {
+          if (leader) tc_commit(bar(b));
+          __syncwarp();
+        };
+        int jl = 0;  // blocks of this item
+        bool prev_first = false;
+        for (int sgi = 0; sgi < nseg && ok; ++sgi) {
+          const int nblk = seg_blocks(ctl, sgi);
+          for (int j = 0; j < nblk && ok; ++j, ++jg, ++jl) {
+            const int st = jg % kStages;
+            ok = wait_warp(bar(kBarKF + st), (jg / kStages) & 1);
+            if (!ok) break;
+            tc_fence_after();
+            issue_qk(0, jg);
+            if (jl > 0) {
+              ok = issue_pv(1, jg - 1, prev_first);
+              if (!ok) break;
+              commit(kBarVE + (jg - 1) % kStages);  // both tiles have read V(jg - 1)
+            }
+            issue_qk(1, jg);
+            commit(kBarKE + st);                     // both tiles have read K(jg)
+            ok = wait_warp(bar(kBarVF + st), (jg / kStages) & 1);
+            if (ok) ok = issue_pv(0, jg, j == 0);
+            prev_first = (j == 0);
+          }
+        }
         if (ok) {
-          const uint32_t dst = base0 + st * kKVBytes;
-          mbar_arrive_expect_tx(bar(full0 + st), ndh * (kKVBytes / 2));
-          for (int h = 0; h < ndh; ++h)
-#pragma unroll
-            for (int p = 0; p < kPgPerBlk; ++p)
-              tma_load_5d_nohint(dst + h * (kKVBytes / 2) + p * (kPage * 128), tm, bar(full0 + st),
-                                 0, 0, dh0 + h, kvh, pgs[p]);
-        }
-      }
-      ok = __shfl_sync(0xffffffffu, ok, 0);
-      sgi = nsgi;
-      j = nj;
-      pg = pg_next;
-    }
-    if (!ok && lane == 0) atomicOr(a.err, SS_DEVERR_TIMEOUT);
-  } else if (warp < 4 && nblk_total > 0) {
-    // ================================ MMA issuer ==================================
-    // The whole warp walks the schedule and waits; one elected lane issues.  Descriptors
-    // are per-operand bases plus compile-time offsets (the start-address field holds
-    // address / 16 in bits 0-13, and no offset here carries out of it).
-    constexpr uint32_t idesc_qk = idesc_bf16_f32(128, kNB, 0, 0);
-    constexpr uint32_t idesc_pv = idesc_bf16_f32(128, kHDp, 0, 1);
-    const bool leader = elect_one();
-    uint64_t dq[kTiles], dk[kStages], dv[kStages];
-#pragma unroll
-    for (int t = 0; t < kTiles; ++t) dq[t] = smem_desc_sw128(sQ + t * kQBytes, 16, 1024);
-#pragma unroll
-    for (int st = 0; st < kStages; ++st) {
-      dk[st] = smem_desc_sw128(sK0 + st * kKVBytes, 16, 1024);
-      dv[st] = smem_desc_sw128(sV0 + st * kKVBytes, kKVBytes / 2, 1024);
-    }
-    bool ok = mbar_wait(bar(kBarQ), 0);
-    // S_t(jg) = Q_t K(jg)^T into columns [128 t, 128 t + 128).
-    auto issue_qk = [&](int t, int jg) {
-      if (leader) {
-        const uint64_t kd = dk[jg % kStages];
-#pragma unroll
-        for (int kk = 0; kk < kHDp / 16; ++kk) {
-          const uint32_t off = ((kk >> 2) * (kKVBytes / 2) + (kk & 3) * 32) >> 4;
-          const uint32_t qoff = ((kk >> 2) * (kQBytes / 2) + (kk & 3) * 32) >> 4;
-          tc_mma_f16(tmem + t * kNB, dq[t] + qoff, kd + off, idesc_qk, kk > 0 ? 1u : 0u);
-        }
-        tc_commit(bar(kBarS + t));
-      }
-      __syncwarp();
-    };
-    // O_t (+)= P_t(jg) V(jg); P_t sits in the first 64 columns of S_t (16 keys = 8
-    // columns per k-step).
-    auto issue_pv = [&](int t, int jg, bool first_of_seg) -> bool {
-      if (!mbar_wait(bar(kBarP + t), jg & 1)) return false;
-      tc_fence_after();
-      if (leader) {
-        const uint64_t vd = dv[jg % kStages];
-#pragma unroll
-        for (int kk = 0; kk < kNB / 16; ++kk)
-          tc_mma_f16_ts(tmem + kColO + t * kHDp, tmem + t * kNB + kk * 8,
-                        vd + ((kk * 16 * 128) >> 4), idesc_pv,
-                        (!first_of_seg || kk > 0) ? 1u : 0u);
-        tc_commit(bar(kBarPV + t));
-      }
-      __syncwarp();
-      return true;
-    };
-    auto commit = [&](int b) {
-      if (leader) tc_commit(bar(b));
-      __syncwarp();
-    };
-    int jg = 0;
-    bool prev_first = false;
-    for (int sgi = 0; sgi < nseg && ok; ++sgi) {
-      const int nblk = seg_blocks(ctl, sgi);
-      for (int j = 0; j < nblk && ok; ++j, ++jg) {
-        const int st = jg % kStages;
-        ok = mbar_wait(bar(kBarKF + st), (jg / kStages) & 1);
-        if (!ok) break;
-        tc_fence_after();
-        issue_qk(0, jg);
-        if (jg > 0) {
           ok = issue_pv(1, jg - 1, prev_first);
-          if (!ok) break;
-          commit(kBarVE + (jg - 1) % kStages);  // both tiles have read V(jg - 1)
+          if (ok) commit(kBarVE + (jg - 1) % kStages);
         }
-        issue_qk(1, jg);
-        commit(kBarKE + st);                     // both tiles have read K(jg)
-        ok = mbar_wait(bar(kBarVF + st), (jg / kStages) & 1);
-        if (ok) ok = issue_pv(0, jg, j == 0);
-        prev_first = (j == 0);
+        if (!ok && lane == 0) {
+          atomicOr(a.err, SS_DEVERR_TIMEOUT);
+          ctl->abort = 1;
+        }
       }
+      tc_fence_before();
     }
-    if (ok) {
-      ok = issue_pv(1, jg - 1, prev_first);
-      if (ok) commit(kBarVE + (jg - 1) % kStages);
-    }
-    if (!ok && lane == 0) atomicOr(a.err, SS_DEVERR_TIMEOUT);
-  } else if (warp >= 4) {
-    // ============== softmax + epilogue (1 row per thread, one tile per warpgroup) ===========
+  } else {
     setmaxnreg_inc<kRegsSoftmax>();
-    const int tt = (warp - 4) >> 2;      // tile of this warpgroup
-    const int wq = warp & 3;             // TMEM lane quadrant of this warp
-    const int row = wq * 32 + lane;      // tile row = token * 8 + head
-    const int rt = tt * kTQT + row / kGroup, rh = row % kGroup;  // window token, head
-    const long long t = t0 + rt;
-    const uint32_t lane_off = static_cast<uint32_t>(wq * 32) << 16;
-    const uint32_t tS = tmem + tt * kNB + lane_off, tO = tmem + kColO + tt * kHDp + lane_off;
-    const float sc = a.scale_log2;
-    int jg = 0;
-    bool ok = true;
-    for (int sgi = 0; sgi < nseg && ok; ++sgi) {
-      const int f = ctl->seg_first[sgi], l = ctl->seg_last[sgi];
-      const bool mine = rt >= f && rt <= l && t < a.T;
-      const int keys = mine ? token_info(a, t, false).L : 0;
-      const int nblk = seg_blocks(ctl, sgi);
-      __nv_bfloat16* op = a.out + t * a.o_st + static_cast<long long>(kvh * kGroup + rh) * a.o_sh;
-      if (nblk == 0) {  // no row of the segment has keys: zero output rows
-        if (mine)
-          for (int dd = 0; dd < kHDp; ++dd) op[dd * a.o_sd] = __float2bfloat16(0.f);
-        continue;
-      }
-      // Rows outside the segment compute on whatever their Q row holds and are discarded,
-      // so they are never masked (this keeps full blocks mask-free for the whole warp).
-      const int lim = mine ? keys : INT_MAX;
-      float m_ref = -CUDART_INF_F, lsum = 0.f;
-      for (int j = 0; j < nblk; ++j, ++jg) {
-        ok = mbar_wait(bar(kBarS + tt), jg & 1);
-        if (!ok) break;
-        tc_fence_after();
-        uint32_t sr[4][32];
+    for (;;) {
+      const ItemInfo it = item_head();
+      if (!it.live) break;
+      const long long t0 = it.t0;
+      const int kvh = it.kvh, nseg = it.nseg;
+      {
+        // ============== softmax + epilogue (1 row per thread, one tile per warpgroup) ===========
+        const int tt = (warp - 4) >> 2;      // tile of this warpgroup
+        const int wq = warp & 3;             // TMEM lane quadrant of this warp
+        const int row = wq * 32 + lane;      // tile row = token * 8 + head
+        const int rt = tt * kTQT + row / kGroup, rh = row % kGroup;  // window token, head
+        const long long t = t0 + rt;
+        const uint32_t lane_off = static_cast<uint32_t>(wq * 32) << 16;
+        const uint32_t tS = tmem + tt * kNB + lane_off, tO = tmem + kColO + tt * kHDp + lane_off;
+        const float sc = a.scale_log2;
+        for (int sgi = 0; sgi < nseg && ok; ++sgi) {
+          const int f = ctl->seg_first[sgi], l = ctl->seg_last[sgi];
+          const bool mine = rt >= f && rt <= l && t < a.T;
+          const int keys = mine ? token_info(a, t, false).L : 0;
+          const int nblk = seg_blocks(ctl, sgi);
+          __nv_bfloat16* op = a.out + t * a.o_st + static_cast<long long>(kvh * kGroup + rh) * a.o_sh;
+          if (nblk == 0) {  // no row of the segment has keys: zero output rows
+            if (mine)
+              for (int dd = 0; dd < kHDp; ++dd) op[dd * a.o_sd] = __float2bfloat16(0.f);
+            continue;
+          }
+          // Rows outside the segment compute on whatever their Q row holds and are discarded,
+          // so they are never masked (this keeps full blocks mask-free for the whole warp).
+          const int lim = mine ? keys : INT_MAX;
+          float m_ref = -CUDART_INF_F, lsum = 0.f;
+          for (int j = 0; j < nblk; ++j, ++jg) {
+            ok = wait_warp(bar(kBarS + tt), jg & 1);
+            if (!ok) break;
+            tc_fence_after();
+            uint32_t sr[4][32];
 #pragma unroll
-        for (int c = 0; c < 4; ++c) tmem_ld32(tS + c * 32, sr[c]);
-        tmem_wait_ld();
-        const int nv = lim - j * kNB;  // valid columns of this row in this block
-        if (!__all_sync(0xffffffffu, nv >= kNB)) {
+            for (int c = 0; c < 4; ++c) tmem_ld32(tS + c * 32, sr[c]);
+            tmem_wait_ld();
+            const int nv = lim - j * kNB;  // valid columns of this row in this block
+            if (!__all_sync(0xffffffffu, nv >= kNB)) {
 #pragma unroll
-          for (int c = 0; c < 4; ++c)
+              for (int c = 0; c < 4; ++c)
 #pragma unroll
-            for (int i = 0; i < 32; ++i)
-              if (c * 32 + i >= nv) sr[c][i] = __float_as_uint(-CUDART_INF_F);
-        }
-        // Row max of the raw scores: four independent chains of three-input maxima.
-        float mc[4];
+                for (int i = 0; i < 32; ++i)
+                  if (c * 32 + i >= nv) sr[c][i] = __float_as_uint(-CUDART_INF_F);
+            }
+            // Row max of the raw scores: four independent chains of three-input maxima.
+            float mc[4];
 #pragma unroll
-        for (int c = 0; c < 4; ++c) {
-          float m = fmaxf(__uint_as_float(sr[c][0]), __uint_as_float(sr[c][1]));
+            for (int c = 0; c < 4; ++c) {
+              float m = fmaxf(__uint_as_float(sr[c][0]), __uint_as_float(sr[c][1]));
 #pragma unroll
-          for (int i = 2; i < 32; i += 2)
-            m = max3(m, __uint_as_float(sr[c][i]), __uint_as_float(sr[c][i + 1]));
-          mc[c] = m;
-        }
-        const float mblk = max3(mc[0], mc[1], fmaxf(mc[2], mc[3])) * sc;  // sc > 0
-        // Keep the reference max unless this block raises it by more than 8 (2^8 in p).
-        const bool raise = mblk > m_ref + 8.f;
-        const float m_new = raise ? mblk : m_ref;
-        const float alpha = raise ? (m_ref == -CUDART_INF_F ? 0.f : ex2(m_ref - m_new)) : 1.f;
-        if (j > 0 && __any_sync(0xffffffffu, raise)) {
-          // Rescale O_t in place.  S_t(jg) completing implies P_t.V(jg - 1) completed (the
-          // MMA thread issued it earlier); the wait below returns at once.
-          ok = mbar_wait(bar(kBarPV + tt), (jg - 1) & 1);
+              for (int i = 2; i < 32; i += 2)
+                m = max3(m, __uint_as_float(sr[c][i]), __uint_as_float(sr[c][i + 1]));
+              mc[c] = m;
+            }
+            const float mblk = max3(mc[0], mc[1], fmaxf(mc[2], mc[3])) * sc;  // sc > 0
+            // Keep the reference max unless this block raises it by more than 8 (2^8 in p).
+            const bool raise = mblk > m_ref + 8.f;
+            const float m_new = raise ? mblk : m_ref;
+            const float alpha = raise ? (m_ref == -CUDART_INF_F ? 0.f : ex2(m_ref - m_new)) : 1.f;
+            if (j > 0 && __any_sync(0xffffffffu, raise)) {
+              // Rescale O_t in place.  S_t(jg) completing implies P_t.V(jg - 1) completed (the
+              // MMA thread issued it earlier); the wait below returns at once.
+              ok = wait_warp(bar(kBarPV + tt), (jg - 1) & 1);
+              if (!ok) break;
+              tc_fence_after();
+#pragma unroll
+              for (int c = 0; c < 4; ++c) {
+                uint32_t orow[32];
+                tmem_ld32(tO + c * 32, orow);
+                tmem_wait_ld();
+#pragma unroll
+                for (int i = 0; i < 32; ++i) orow[i] = __float_as_uint(__uint_as_float(orow[i]) * alpha);
+                tmem_st32(tO + c * 32, orow);
+              }
+            }
+            m_ref = m_new;
+            const float ms = m_ref == -CUDART_INF_F ? 0.f : m_ref;
+            const uint64_t sc2 = f2pack(sc, sc), nms2 = f2pack(-ms, -ms);
+            uint64_t acc[4] = {0, 0, 0, 0};  // four independent packed partial row sums
+            // p = 2^(s sc - m): paired fma, then the hardware exponential for most pairs and the
+            // polynomial on the FMA pipe for one pair in kPolyEvery; P as bf16 pairs over the
+            // first 64 columns of S_t (column c holds keys 2c, 2c + 1).
+#pragma unroll
+            for (int h2 = 0; h2 < 2; ++h2) {
+              uint32_t pk[32];
+#pragma unroll
+              for (int i = 0; i < 32; ++i) {
+                const int k0 = h2 * 64 + 2 * i;
+                const uint64_t x2 = fma2(f2pack(__uint_as_float(sr[k0 >> 5][k0 & 31]),
+                                                __uint_as_float(sr[(k0 + 1) >> 5][(k0 + 1) & 31])),
+                                         sc2, nms2);
+                uint64_t p2;
+                if ((i % kPolyEvery) == kPolyEvery - 1) {
+                  p2 = exp2_poly2(x2);
+                } else {
+                  float x0, x1;
+                  f2unpack(x2, x0, x1);
+                  p2 = f2pack(ex2(x0), ex2(x1));
+                }
+                acc[i & 3] = add2(acc[i & 3], p2);
+                float p0, p1;
+                f2unpack(p2, p0, p1);
+                pk[i] = pack_bf16(p0, p1);
+              }
+              tmem_st32(tS + h2 * 32, pk);
+              tmem_wait_st();  // (also orders a rescale of O_t before the P.V that reads it)
+              tc_fence_before();
+              mbar_arrive(bar((h2 ? kBarP : kBarPH) + tt));
+            }
+            float s0, s1;
+            f2unpack(add2(add2(acc[0], acc[1]), add2(acc[2], acc[3])), s0, s1);
+            lsum = lsum * alpha + (s0 + s1);
+          }
+          if (!ok) break;
+          // ---- epilogue: O_t / l -> bf16 ---------------------------------------------------
+          ok = wait_warp(bar(kBarPV + tt), (jg - 1) & 1);
           if (!ok) break;
           tc_fence_after();
+          const float inv = lsum > 0.f ? 1.f / lsum : 0.f;
+          const bool vec = mine && a.o_sd == 1 && ((reinterpret_cast<uintptr_t>(op) & 15) == 0);
 #pragma unroll
           for (int c = 0; c < 4; ++c) {
             uint32_t orow[32];
             tmem_ld32(tO + c * 32, orow);
             tmem_wait_ld();
+            if (mine) {
+              if (vec) {
 #pragma unroll
-            for (int i = 0; i < 32; ++i) orow[i] = __float_as_uint(__uint_as_float(orow[i]) * alpha);
-            tmem_st32(tO + c * 32, orow);
-          }
-        }
-        m_ref = m_new;
-        const float ms = m_ref == -CUDART_INF_F ? 0.f : m_ref;
-        const uint64_t sc2 = f2pack(sc, sc), nms2 = f2pack(-ms, -ms);
-        uint64_t acc[4] = {0, 0, 0, 0};  // four independent packed partial row sums
-        // p = 2^(s sc - m): paired fma, then the hardware exponential for most pairs and the
-        // polynomial on the FMA pipe for one pair in kPolyEvery; P as bf16 pairs over the
-        // first 64 columns of S_t (column c holds keys 2c, 2c + 1).
+                for (int q8 = 0; q8 < 4; ++q8) {
+                  uint4 v;
+                  v.x = pack_bf16(__uint_as_float(orow[q8 * 8 + 0]) * inv, __uint_as_float(orow[q8 * 8 + 1]) * inv);
+                  v.y = pack_bf16(__uint_as_float(orow[q8 * 8 + 2]) * inv, __uint_as_float(orow[q8 * 8 + 3]) * inv);
+                  v.z = pack_bf16(__uint_as_float(orow[q8 * 8 + 4]) * inv, __uint_as_float(orow[q8 * 8 + 5]) * inv);
+                  v.w = pack_bf16(__uint_as_float(orow[q8 * 8 + 6]) * inv, __uint_as_float(orow[q8 * 8 + 7]) * inv);
+                  *reinterpret_cast<uint4*>(op + c * 32 + q8 * 8) = v;
+                }
+              } else {
 #pragma unroll
-        for (int h2 = 0; h2 < 2; ++h2) {
-          uint32_t pk[32];
-#pragma unroll
-          for (int i = 0; i < 32; ++i) {
-            const int k0 = h2 * 64 + 2 * i;
-            const uint64_t x2 = fma2(f2pack(__uint_as_float(sr[k0 >> 5][k0 & 31]),
-                                            __uint_as_float(sr[(k0 + 1) >> 5][(k0 + 1) & 31])),
-                                     sc2, nms2);
-            uint64_t p2;
-            if ((i % kPolyEvery) == kPolyEvery - 1) {
-              p2 = exp2_poly2(x2);
-            } else {
-              float x0, x1;
-              f2unpack(x2, x0, x1);
-              p2 = f2pack(ex2(x0), ex2(x1));
+                for (int i = 0; i < 32; ++i)
+                  op[static_cast<long long>(c * 32 + i) * a.o_sd] = __float2bfloat16(__uint_as_float(orow[i]) * inv);
+              }
             }
-            acc[i & 3] = add2(acc[i & 3], p2);
-            float p0, p1;
-            f2unpack(p2, p0, p1);
-            pk[i] = pack_bf16(p0, p1);
           }
-          tmem_st32(tS + h2 * 32, pk);
+          tc_fence_before();  // O_t reads complete before the next segment's P.V overwrites O_t
         }
-        tmem_wait_st();
-        tc_fence_before();
-        mbar_arrive(bar(kBarP + tt));
-        float s0, s1;
-        f2unpack(add2(add2(acc[0], acc[1]), add2(acc[2], acc[3])), s0, s1);
-        lsum = lsum * alpha + (s0 + s1);
-      }
-      if (!ok) break;
-      // ---- epilogue: O_t / l -> bf16 ---------------------------------------------------
-      ok = mbar_wait(bar(kBarPV + tt), (jg - 1) & 1);
-      if (!ok) break;
-      tc_fence_after();
-      const float inv = lsum > 0.f ? 1.f / lsum : 0.f;
-      const bool vec = mine && a.o_sd == 1 && ((reinterpret_cast<uintptr_t>(op) & 15) == 0);
-#pragma unroll
-      for (int c = 0; c < 4; ++c) {
-        uint32_t orow[32];
-        tmem_ld32(tO + c * 32, orow);
-        tmem_wait_ld();
-        if (mine) {
-          if (vec) {
-#pragma unroll
-            for (int q8 = 0; q8 < 4; ++q8) {
-              uint4 v;
-              v.x = pack_bf16(__uint_as_float(orow[q8 * 8 + 0]) * inv, __uint_as_float(orow[q8 * 8 + 1]) * inv);
-              v.y = pack_bf16(__uint_as_float(orow[q8 * 8 + 2]) * inv, __uint_as_float(orow[q8 * 8 + 3]) * inv);
-              v.z = pack_bf16(__uint_as_float(orow[q8 * 8 + 4]) * inv, __uint_as_float(orow[q8 * 8 + 5]) * inv);
-              v.w = pack_bf16(__uint_as_float(orow[q8 * 8 + 6]) * inv, __uint_as_float(orow[q8 * 8 + 7]) * inv);
-              *reinterpret_cast<uint4*>(op + c * 32 + q8 * 8) = v;
-            }
-          } else {
-#pragma unroll
-            for (int i = 0; i < 32; ++i)
-              op[static_cast<long long>(c * 32 + i) * a.o_sd] = __float2bfloat16(__uint_as_float(orow[i]) * inv);
-          }
+        if (!ok && lane == 0) {
+          atomicOr(a.err, SS_DEVERR_TIMEOUT);
+          ctl->abort = 1;
         }
       }
-      tc_fence_before();  // O_t reads complete before the next segment's P.V overwrites O_t
+      tc_fence_before();  // this item's TMEM accesses are ordered before the next item's
     }
-    if (!ok && lane == 0) atomicOr(a.err, SS_DEVERR_TIMEOUT);
   }
   // ---- teardown ------------------------------------------------------------------------
-  tc_fence_before();
   __syncthreads();
   if (warp == 0) {
     tc_fence_after();
     tmem_dealloc(tmem, kTmemCols);
   }
+  if (tid == 0) {  // the last CTA out returns the work counter to zero for the next launch
+    __threadfence();
+    if (atomicAdd(sched + 1, 1u) == gridDim.x - 1) {
+      atomicExch(sched, 0u);
+      atomicExch(sched + 1, 0u);
+    }
+  }
   // This grid completes only after the decode grid before it (programmatic launch chain),
   // so the merge kernel that waits on this grid also waits on the decode grid.
   griddep_wait();
+}
+
+// SMs of the current device (the persistent grid has one CTA per SM).
+int sm_count() {
+  static std::mutex mu;
+  static int cache[64] = {0};
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return 148;
+  std::lock_guard<std::mutex> lock(mu);
+  if (cache[dev] == 0 &&
+      cudaDeviceGetAttribute(&cache[dev], cudaDevAttrMultiProcessorCount, dev) != cudaSuccess)
+    cache[dev] = 148;
+  return cache[dev];
 }
 
 // The setmaxnreg split needs the kernel to launch with kLaunchRegs registers per thread.
@@ -547,7 +683,8 @@ cudaError_t launch_prefill(const CUtensorMap& tmQ, const CUtensorMap& tmK, const
   });
   if (attr_err != cudaSuccess) return attr_err;
   cudaLaunchConfig_t cfg = {};
-  cfg.gridDim = dim3(static_cast<unsigned>((a.T + kTQ - 1) / kTQ), a.KVH);
+  const long long items = (a.T + kTQ - 1) / kTQ * a.KVH;
+  cfg.gridDim = dim3(static_cast<unsigned>(std::min<long long>(items, sm_count())));
   cfg.blockDim = dim3(kThreadsP);
   cfg.dynamicSmemBytes = kSmemP;
   cfg.stream = stream;

@@ -349,3 +349,21 @@ def test_prefill_tiles_tp2_layout_against_oracle(dev):
     out, ref, path = _ragged_rows_case(dev, [(1000, 300), (4000, 1), (5, 40)], 8, 1, seed=33)
     assert path == 3
     check_close(out, ref)
+
+
+def test_prefill_work_queue_spans_more_items_than_sms(dev):
+    """More (window, KV head) work items than SMs, so CTAs take several items each from the
+    workspace work counter; repeated and interleaved calls check that every launch leaves
+    the counter at zero (a stale counter would skip items and leave rows unwritten)."""
+    g = torch.Generator().manual_seed(5)
+    prefill = [(int(c), 512) for c in torch.randint(0, 1025, (12,), generator=g)]
+    decode = [(int(c) - 1, 1) for c in torch.randint(64, 2049, (8,), generator=g)]
+    rows = decode[:4] + prefill + decode[4:]
+    out, ref, path = _ragged_rows_case(dev, rows, 16, 2, seed=34)
+    assert path == 3
+    check_close(out, ref)
+    small, small_ref, _ = _ragged_rows_case(dev, [(300, 40), (10, 1), (0, 33)], 16, 2, seed=35)
+    check_close(small, small_ref)
+    again, _, _ = _ragged_rows_case(dev, rows, 16, 2, seed=34)
+    assert torch.equal(again, out)
+    assert K.device_errors(dev) == 0
