@@ -85,6 +85,34 @@ SS_API int ss_kv_append(const void* k, const int64_t k_strides[3], const void* v
                  int head_dim, void* workspace, void* stream);
 
 /*
+ * Rotary position embedding of q and k fused with the slot-mapped KV append.  Replaces
+ *     q, k = apply_rope(q, k, cos, sin, positions)   (shardserve/math.py:28-38, model.py:25)
+ *     cache.write(layer, k, v, slots)                 (shardserve/cache.py:47-49, model.py:32)
+ * in one launch, bit-exact with torch's bf16 arithmetic (one bf16 rounding per multiply and
+ * per add, cos / sin rows rounded to bf16 first, math.py:36-38).
+ * q, q_out     : bf16 [tokens, heads, head_dim]; q_out receives the rotated queries and may
+ *                be q itself (rotation in place)
+ * k, v         : bf16 [tokens, kv_heads, head_dim]: unrotated keys, values
+ * cos_table, sin_table: fp32 [table_rows, head_dim] (the caller's tables, as built by
+ *                math.build_rope_cache, math.py:12-20), element strides cos/sin_strides
+ * positions    : [tokens] int32 / int64 row of each token in the tables
+ * k_pool/v_pool, slots: as ss_kv_append; the rotated k and v land in row slot % 16 of page
+ *                slot / 16
+ * head_dim even.  A token whose position lies outside [0, table_rows) is skipped entirely
+ * (SS_DEVERR_POS); a slot outside the pool skips that token's append (SS_DEVERR_SLOT).
+ * workspace    : optional error word, as ss_kv_append.
+ */
+SS_API int ss_rope_kv_append(const void* q, const int64_t q_strides[3], void* q_out,
+                      const int64_t q_out_strides[3], const void* k, const int64_t k_strides[3],
+                      const void* v, const int64_t v_strides[3], const float* cos_table,
+                      const int64_t cos_strides[2], const float* sin_table,
+                      const int64_t sin_strides[2], int64_t table_rows, const void* positions,
+                      int positions_is_int64, void* k_pool, const int64_t k_pool_strides[4],
+                      void* v_pool, const int64_t v_pool_strides[4], const void* slots,
+                      int slots_is_int64, int64_t tokens, int heads, int kv_heads, int head_dim,
+                      int64_t num_pages, void* workspace, void* stream);
+
+/*
  * Workspace size (bytes) that ss_ragged_paged_attention needs on `device` for this geometry.
  * Byte 0..3 of the workspace is the device error word (zero it to start clean).  Bytes
  * 64..71 hold the chunked-prefill work counter: they must be zero before the first call (a

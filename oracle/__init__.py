@@ -12,3 +12,4 @@ from .ragged_attention import (  # noqa: F401
     ragged_attention,
     token_slots,
 )
+from .rope import apply_rope_bits, rope_tables  # noqa: F401

@@ -38,6 +38,10 @@ SIGNATURES = {
     "ss_kv_append": (ctypes.c_int, [
         _vp, _i64p, _vp, _i64p, _vp, _i64p, _vp, _i64p, _vp, ctypes.c_int,
         ctypes.c_int64, ctypes.c_int64, ctypes.c_int, ctypes.c_int, _vp, _vp]),
+    "ss_rope_kv_append": (ctypes.c_int, [
+        _vp, _i64p, _vp, _i64p, _vp, _i64p, _vp, _i64p, _vp, _i64p, _vp, _i64p, ctypes.c_int64,
+        _vp, ctypes.c_int, _vp, _i64p, _vp, _i64p, _vp, ctypes.c_int, ctypes.c_int64,
+        ctypes.c_int, ctypes.c_int, ctypes.c_int, ctypes.c_int64, _vp, _vp]),
     "ss_attention_workspace_bytes": (ctypes.c_int, [
         ctypes.c_int, ctypes.c_int64, ctypes.c_int, ctypes.c_int, ctypes.c_int,
         ctypes.POINTER(ctypes.c_size_t)]),

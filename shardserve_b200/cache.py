@@ -15,7 +15,7 @@ from __future__ import annotations
 
 import math
 
-from .kernel import KernelUnsupported, kv_append
+from .kernel import KernelUnsupported, kv_append, rope_kv_append
 
 
 class Blocks:
@@ -71,3 +71,9 @@ class Cache:
     def write(self, layer, k, v, slots):
         """Appends k, v [tokens, kv_heads, head_dim] at `slots` of `layer` (cache.py:47-49)."""
         kv_append(self.k[layer], self.v[layer], k, v, slots)
+
+    def write_rope(self, layer, q, k, v, cos, sin, positions, slots, out=None):
+        """Rotates q and k with RoPE at `positions` (math.py:28-38) and appends the rotated
+        k and v at `slots` of `layer` in one launch; returns the rotated q."""
+        return rope_kv_append(q, k, v, cos, sin, positions, self.k[layer], self.v[layer], slots,
+                              out=out)

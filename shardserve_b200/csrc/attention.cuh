@@ -155,6 +155,24 @@ struct AppendArgs {
 };
 cudaError_t launch_kv_append(const AppendArgs& a, bool vectorised, cudaStream_t stream);
 
+// Rotary position embedding of q and k fused with the slot-mapped K/V append
+// (rope_append.cu).  The append part reuses AppendArgs (k = the unrotated keys).
+struct RopeArgs {
+  AppendArgs app;
+  const __nv_bfloat16* q;
+  long long q_st, q_sh, q_sd;
+  __nv_bfloat16* qo;  // rotated queries (may equal q)
+  long long qo_st, qo_sh, qo_sd;
+  const float* cos;
+  const float* sin;
+  long long cos_sr, cos_sd, sin_sr, sin_sd;
+  long long rows;  // table rows: positions must lie in [0, rows)
+  const void* pos;
+  int pos64;
+  int H;
+};
+cudaError_t launch_rope_append(const RopeArgs& r, bool vectorised, cudaStream_t stream);
+
 // Sets the text ss_last_error_message() returns on this thread (printf-style).
 void set_error_message(const char* fmt, ...);
 

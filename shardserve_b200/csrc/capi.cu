@@ -188,6 +188,77 @@ int ss_kv_append(const void* k, const int64_t k_strides[3], const void* v,
   return SS_OK;
 }
 
+int ss_rope_kv_append(const void* q, const int64_t q_strides[3], void* q_out,
+                      const int64_t q_out_strides[3], const void* k, const int64_t k_strides[3],
+                      const void* v, const int64_t v_strides[3], const float* cos_table,
+                      const int64_t cos_strides[2], const float* sin_table,
+                      const int64_t sin_strides[2], int64_t table_rows, const void* positions,
+                      int positions_is_int64, void* k_pool, const int64_t k_pool_strides[4],
+                      void* v_pool, const int64_t v_pool_strides[4], const void* slots,
+                      int slots_is_int64, int64_t tokens, int heads, int kv_heads, int head_dim,
+                      int64_t num_pages, void* workspace, void* stream) {
+  if (tokens < 0) return fail(SS_ERR_INVALID, "tokens must be >= 0");
+  if (tokens == 0) return SS_OK;
+  if (!q || !q_out || !k || !v || !cos_table || !sin_table || !positions || !k_pool ||
+      !v_pool || !slots || !q_strides || !q_out_strides || !k_strides || !v_strides ||
+      !cos_strides || !sin_strides || !k_pool_strides || !v_pool_strides)
+    return fail(SS_ERR_INVALID, "null pointer argument");
+  if (heads < 1 || kv_heads < 1 || num_pages < 1 || table_rows < 1)
+    return fail(SS_ERR_INVALID, "heads, kv_heads, num_pages and table_rows must be positive");
+  if (head_dim < 2 || head_dim % 2)
+    return fail(SS_ERR_INVALID, "head_dim must be even (RoPE rotates the two halves)");
+  if (!finite_nonneg_strides(q_strides, 3) || !finite_nonneg_strides(q_out_strides, 3) ||
+      !finite_nonneg_strides(k_strides, 3) || !finite_nonneg_strides(v_strides, 3) ||
+      !finite_nonneg_strides(cos_strides, 2) || !finite_nonneg_strides(sin_strides, 2) ||
+      !finite_nonneg_strides(k_pool_strides, 4) || !finite_nonneg_strides(v_pool_strides, 4))
+    return fail(SS_ERR_INVALID, "negative strides are not supported");
+  ss::RopeArgs r;
+  ss::AppendArgs& a = r.app;
+  a.k = static_cast<const __nv_bfloat16*>(k);
+  a.k_st = k_strides[0]; a.k_sh = k_strides[1]; a.k_sd = k_strides[2];
+  a.v = static_cast<const __nv_bfloat16*>(v);
+  a.v_st = v_strides[0]; a.v_sh = v_strides[1]; a.v_sd = v_strides[2];
+  a.kp = static_cast<__nv_bfloat16*>(k_pool);
+  a.kp_sn = k_pool_strides[0]; a.kp_ss = k_pool_strides[1];
+  a.kp_sh = k_pool_strides[2]; a.kp_sd = k_pool_strides[3];
+  a.vp = static_cast<__nv_bfloat16*>(v_pool);
+  a.vp_sn = v_pool_strides[0]; a.vp_ss = v_pool_strides[1];
+  a.vp_sh = v_pool_strides[2]; a.vp_sd = v_pool_strides[3];
+  a.slots = slots;
+  a.slots64 = slots_is_int64 ? 1 : 0;
+  a.T = tokens;
+  a.N = num_pages;
+  a.KVH = kv_heads;
+  a.D = head_dim;
+  a.err = workspace ? static_cast<unsigned*>(workspace) : nullptr;
+  r.q = static_cast<const __nv_bfloat16*>(q);
+  r.q_st = q_strides[0]; r.q_sh = q_strides[1]; r.q_sd = q_strides[2];
+  r.qo = static_cast<__nv_bfloat16*>(q_out);
+  r.qo_st = q_out_strides[0]; r.qo_sh = q_out_strides[1]; r.qo_sd = q_out_strides[2];
+  r.cos = cos_table;
+  r.cos_sr = cos_strides[0]; r.cos_sd = cos_strides[1];
+  r.sin = sin_table;
+  r.sin_sr = sin_strides[0]; r.sin_sd = sin_strides[1];
+  r.rows = table_rows;
+  r.pos = positions;
+  r.pos64 = positions_is_int64 ? 1 : 0;
+  r.H = heads;
+  auto vec_ok = [](const void* p, const int64_t* st, int n, int mult) {
+    if ((reinterpret_cast<uintptr_t>(p) & 15) != 0 || st[n - 1] != 1) return false;
+    for (int i = 0; i < n - 1; ++i)
+      if (st[i] % mult) return false;
+    return true;
+  };
+  const bool vec = (head_dim % 16 == 0) && vec_ok(q, q_strides, 3, 8) &&
+                   vec_ok(q_out, q_out_strides, 3, 8) && vec_ok(k, k_strides, 3, 8) &&
+                   vec_ok(v, v_strides, 3, 8) && vec_ok(k_pool, k_pool_strides, 4, 8) &&
+                   vec_ok(v_pool, v_pool_strides, 4, 8) && vec_ok(cos_table, cos_strides, 2, 4) &&
+                   vec_ok(sin_table, sin_strides, 2, 4);
+  const cudaError_t e = ss::launch_rope_append(r, vec, static_cast<cudaStream_t>(stream));
+  if (e != cudaSuccess) return cuda_fail(e, "rope_kv_append launch");
+  return SS_OK;
+}
+
 int ss_attention_workspace_bytes(int device, int64_t tokens, int heads, int kv_heads,
                                  int head_dim, size_t* bytes) {
   if (!bytes) return fail(SS_ERR_INVALID, "bytes is null");

@@ -214,3 +214,73 @@ def kv_append(k_pool_layer: Any, v_pool_layer: Any, k: Any, v: Any, slots: Any) 
         raise KernelUnsupported(_native.last_error())
     if rc != _native.SS_OK:
         raise RuntimeError(f"ss_kv_append: {_native.last_error()}")
+
+
+def rope_kv_append(q: Any, k: Any, v: Any, cos: Any, sin: Any, positions: Any,
+                   k_pool_layer: Any, v_pool_layer: Any, slots: Any, out: Any = None) -> Any:
+    """One launch for `q, k = apply_rope(q, k, cos, sin, positions)` (shardserve/math.py:28-38,
+    model.py:25) followed by `Cache.write(layer, k, v, slots)` (cache.py:47-49, model.py:32).
+
+    q [tokens, heads, D], k / v [tokens, kv_heads, D] bf16; cos / sin fp32 [rows, D] (the
+    tables of math.build_rope_cache); positions / slots int32 or int64 [tokens].  Returns the
+    rotated q (in `out` if given; `out` may be q itself).  Bit-exact with the reference's
+    bf16 arithmetic."""
+    import torch
+
+    if k_pool_layer.device.type != "cuda":
+        raise KernelUnsupported("RoPE + KV append requires CUDA pools")
+    if k_pool_layer.dtype != torch.bfloat16 or v_pool_layer.dtype != torch.bfloat16:
+        raise KernelUnsupported("KV pools must be BF16")
+    if k_pool_layer.shape != v_pool_layer.shape or k_pool_layer.dim() != 4 \
+            or k_pool_layer.shape[1] != SUPPORTED_BLOCK_SIZE:
+        raise KernelUnsupported("ragged K/V pools must have identical rank-4 shapes")
+    kv_heads, head_dim = k_pool_layer.shape[2], k_pool_layer.shape[3]
+    if q.dim() != 3 or q.shape[2] != head_dim or q.dtype != torch.bfloat16:
+        raise KernelUnsupported(f"q must be BF16 [tokens, heads, {head_dim}]")
+    if k.dim() != 3 or tuple(k.shape[1:]) != (kv_heads, head_dim) or k.shape != v.shape:
+        raise KernelUnsupported(
+            f"k/v must be [tokens, {kv_heads}, {head_dim}], got {tuple(k.shape)}/{tuple(v.shape)}")
+    if k.dtype != torch.bfloat16 or v.dtype != torch.bfloat16:
+        raise KernelUnsupported("k/v must be BF16")
+    if q.shape[0] != k.shape[0] or q.shape[1] % kv_heads:
+        raise KernelUnsupported("q and k/v must have the same tokens and a whole GQA group")
+    if head_dim % 2:
+        raise KernelUnsupported("RoPE needs an even head_dim")
+    for name, t in (("cos", cos), ("sin", sin)):
+        if t.dtype != torch.float32 or t.dim() != 2 or t.shape[1] != head_dim:
+            raise KernelUnsupported(f"{name} must be float32 [rows, {head_dim}]")
+    if cos.shape != sin.shape:
+        raise KernelUnsupported("cos and sin tables must have the same shape")
+    for name, t in (("v_pool_layer", v_pool_layer), ("q", q), ("k", k), ("v", v), ("cos", cos),
+                    ("sin", sin), ("positions", positions), ("slots", slots)):
+        if t.device != k_pool_layer.device:
+            raise KernelUnsupported(f"{name} must be on {k_pool_layer.device}")
+    tokens = q.shape[0]
+    if slots.numel() != tokens or positions.numel() != tokens:
+        raise KernelUnsupported("one position and one slot are required per token")
+    p64 = _index_flag(positions, "positions")
+    s64 = _index_flag(slots, "slots")
+    pos = positions.reshape(-1)
+    sl = slots.reshape(-1)
+    pos = pos if pos.is_contiguous() else pos.contiguous()
+    sl = sl if sl.is_contiguous() else sl.contiguous()
+    if out is None:
+        out = torch.empty_like(q)
+    elif out.shape != q.shape or out.dtype != torch.bfloat16 or out.device != q.device:
+        raise KernelUnsupported("out must be a BF16 tensor shaped like q on q's device")
+    ws = _workspaces.get(k_pool_layer.device.index)
+    stream = torch.cuda.current_stream(k_pool_layer.device).cuda_stream
+    rc = _native.lib().ss_rope_kv_append(
+        q.data_ptr(), _native.strides(q.stride()), out.data_ptr(), _native.strides(out.stride()),
+        k.data_ptr(), _native.strides(k.stride()), v.data_ptr(), _native.strides(v.stride()),
+        cos.data_ptr(), _native.strides(cos.stride()), sin.data_ptr(),
+        _native.strides(sin.stride()), cos.shape[0], pos.data_ptr(), p64,
+        k_pool_layer.data_ptr(), _native.strides(k_pool_layer.stride()),
+        v_pool_layer.data_ptr(), _native.strides(v_pool_layer.stride()),
+        sl.data_ptr(), s64, tokens, q.shape[1], kv_heads, head_dim, k_pool_layer.shape[0],
+        ws.data_ptr() if ws is not None else None, stream)
+    if rc == _native.SS_ERR_INVALID:
+        raise KernelUnsupported(_native.last_error())
+    if rc != _native.SS_OK:
+        raise RuntimeError(f"ss_rope_kv_append: {_native.last_error()}")
+    return out
