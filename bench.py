@@ -9,9 +9,11 @@ the step's new K/V rows (Cache.write) + ragged_attention_direct over the batch.
 Other workloads (`--workload`, one JSON line each; same timing rules):
   mixed     8 prefill chunks x 512 tokens on cached context U[0, 2048] (causal inside the
             chunk) + 56 decode rows with context U[256, 4096], one ragged launch per step
+  rope      one decode layer's RoPE of q / k + K/V append for the batch-64 workload: the
+            fused launch against the same work as separate torch ops
   layers36  256 sequences (split over the GPUs) with context U[512, 8192]; one step = the
-            36 layers' append + attention, per-layer pools; q/k/v come from random-init
-            Qwen2.5-3B projections of N(0,1) hidden states with RoPE theta 1e6
+            36 layers' fused RoPE (theta 1e6) + append and attention, per-layer pools; q/k/v
+            come from random-init Qwen2.5-3B projections of N(0,1) hidden states
   tp2long   the reference's TP2 per-rank layout (8 query heads, 1 KV head): 32 sequences
             with context U[16384, 32768] per TP2 pair (split over pairs on 4/8 GPUs), pool
             filling ~60 % of HBM with scattered pages
@@ -58,7 +60,7 @@ def parse():
     p.add_argument("--steps", type=int, default=4000)
     p.add_argument("--warmup", type=int, default=200)
     p.add_argument("--impl", choices=["ours", "reference"], default="ours")
-    p.add_argument("--workload", choices=["decode64", "mixed", "layers36", "tp2long"],
+    p.add_argument("--workload", choices=["decode64", "mixed", "layers36", "tp2long", "rope"],
                    default="decode64")
     p.add_argument("--replicas", type=int, default=4, help="batches rotated to defeat L2")
     p.add_argument("--graph-steps", type=int, default=100, help="steps per captured graph")
@@ -452,9 +454,83 @@ def run_mixed(args, rank, world, dist, h):
             "data": "synthetic", "scaling": "weak"}
 
 
+def rope_tables(head_dim, max_len, theta, dev):
+    """fp32 cos / sin tables [max_len, head_dim] laid out as shardserve/math.py:12-20."""
+    import torch
+
+    inv = 1.0 / (theta ** (torch.arange(0, head_dim, 2, device=dev, dtype=torch.float32)
+                           / head_dim))
+    ang = torch.arange(max_len, device=dev, dtype=torch.float32)[:, None] * inv[None, :]
+    emb = torch.cat((ang, ang), dim=-1)
+    return emb.cos(), emb.sin()
+
+
+def run_rope(args, rank, world, dist, h):
+    """RoPE of q / k + KV append for one decode layer of the batch-64 workload: the fused
+    launch against the same work as separate torch ops (the reference's apply_rope
+    expression, math.py:36-38, then two index_copy_ appends, cache.py:47-49)."""
+    import torch
+
+    import shardserve_b200 as sb
+    from shardserve_b200.workloads import decode_batch
+
+    lengths = rank_lengths(world, rank, args.seed)
+    R = max(1, args.replicas)
+    batches = [decode_batch(lengths, HEADS, KV_HEADS, HEAD_DIM, seed=args.seed + 7 * r + rank,
+                            device=h.dev) for r in range(R)]
+    cos, sin = rope_tables(HEAD_DIM, 4096, 1e6, h.dev)
+    T = batches[0].tokens
+    qouts = [torch.empty_like(b.q) for b in batches]
+
+    def fused(i):
+        b, qo = batches[i], qouts[i]
+        return lambda: sb.rope_kv_append(b.q, b.k_new, b.v_new, cos, sin, b.positions, b.k_pool,
+                                         b.v_pool, b.slots, out=qo)
+
+    def unfused(i):
+        b = batches[i]
+
+        def f():
+            c = cos[b.positions][:, None, :].to(torch.bfloat16)
+            s_ = sin[b.positions][:, None, :].to(torch.bfloat16)
+            half = HEAD_DIM // 2
+            rq = torch.cat((-b.q[..., half:], b.q[..., :half]), -1)
+            rk = torch.cat((-b.k_new[..., half:], b.k_new[..., :half]), -1)
+            q2 = (b.q * c) + (rq * s_)
+            k2 = (b.k_new * c) + (rk * s_)
+            b.k_pool.flatten(0, 1).index_copy_(0, b.slots, k2)
+            b.v_pool.flatten(0, 1).index_copy_(0, b.slots, b.v_new)
+            return q2
+        return f
+
+    fns = [fused(i) for i in range(R)]
+    for f in fns:
+        f()
+    torch.cuda.synchronize()
+    ms, _ = h.run_steps(fns, args.steps, args.warmup)
+    ms = h.max_over_ranks(ms)
+    ufns = [unfused(i) for i in range(R)]
+    for f in ufns:
+        f()
+    torch.cuda.synchronize()
+    ums, _ = h.run_steps(ufns, args.steps, args.warmup)
+    ums = h.max_over_ranks(ums)
+    us, uus = ms * 1e3 / args.steps, ums * 1e3 / args.steps
+    nbytes = T * (2 * HEADS + 4 * KV_HEADS) * HEAD_DIM * 2 + T * 2 * HEAD_DIM * 4 + T * 16
+    peak, _, kind = peaks()
+    return {"metric": "fused RoPE+KV-append us per decode layer", "workload": "rope",
+            "value": us, "unit": "us", "higher_is_better": False, "n_gpus": world,
+            "steps": args.steps, "warmup": args.warmup, "tokens_per_gpu_step": T,
+            "unfused_torch_us": uus, "speedup_vs_unfused": uus / us,
+            "bytes_per_call": nbytes, "hbm_frac": nbytes / (us * 1e-6) / 1e9 / peak,
+            "bound": "launch latency (bytes per call are ~1 MB)", "peak_kind": kind,
+            "dtype": "bf16", "data": "synthetic", "scaling": "weak"}
+
+
 def run_layers36(args, rank, world, dist, h):
     """36 layers of decode attention for 256 sequences (split over the GPUs): q/k/v from
-    random-init projections of N(0,1) hidden states with RoPE (theta 1e6)."""
+    random-init projections of N(0,1) hidden states; each layer's step rotates q/k with RoPE
+    (theta 1e6) and appends k/v in one launch, then runs attention."""
     import torch
     import torch.nn.functional as F
 
@@ -471,15 +547,7 @@ def run_layers36(args, rank, world, dist, h):
     dev = h.dev
     gen = torch.Generator(device=dev).manual_seed(args.seed + 99)
     x = torch.randn(T, hidden, generator=gen, device=dev).to(torch.bfloat16)
-    inv = 1.0 / (1e6 ** (torch.arange(0, HEAD_DIM, 2, device=dev, dtype=torch.float32) / HEAD_DIM))
-    ang = b.positions.float()[:, None] * inv[None, :]
-    cos, sin = torch.cat([ang, ang], -1).cos()[:, None], torch.cat([ang, ang], -1).sin()[:, None]
-
-    def rope(t):
-        half = t.shape[-1] // 2
-        rot = torch.cat((-t[..., half:], t[..., :half]), -1)
-        return (t.float() * cos + rot.float() * sin).to(torch.bfloat16)
-
+    cos, sin = rope_tables(HEAD_DIM, 8192, 1e6, dev)
     qs, ks, vs = [], [], []
     for _ in range(layers):
         w = lambda o: (torch.randn(o, hidden, generator=gen, device=dev) * hidden ** -0.5).to(torch.bfloat16)
@@ -487,14 +555,16 @@ def run_layers36(args, rank, world, dist, h):
         q = F.linear(x, w(HEADS * HEAD_DIM), bias(HEADS * HEAD_DIM)).view(T, HEADS, HEAD_DIM)
         k = F.linear(x, w(KV_HEADS * HEAD_DIM), bias(KV_HEADS * HEAD_DIM)).view(T, KV_HEADS, HEAD_DIM)
         v = F.linear(x, w(KV_HEADS * HEAD_DIM), bias(KV_HEADS * HEAD_DIM)).view(T, KV_HEADS, HEAD_DIM)
-        qs.append(rope(q).contiguous())
-        ks.append(rope(k).contiguous())
+        qs.append(q.contiguous())
+        ks.append(k.contiguous())
         vs.append(v.contiguous())
+    qrot = torch.empty_like(qs[0])
 
-    def step():
+    def step():  # per layer: RoPE(q, k) + append (one launch), then attention
         for l in range(layers):
-            sb.kv_append(b.k_pool[l], b.v_pool[l], ks[l], vs[l], b.slots)
-            sb.ragged_attention_direct(qs[l], b.k_pool[l], b.v_pool[l], b.block_tables,
+            sb.rope_kv_append(qs[l], ks[l], vs[l], cos, sin, b.positions, b.k_pool[l],
+                              b.v_pool[l], b.slots, out=qrot)
+            sb.ragged_attention_direct(qrot, b.k_pool[l], b.v_pool[l], b.block_tables,
                                        b.seq_ids, b.positions, SCALE)
 
     step()
@@ -508,7 +578,7 @@ def run_layers36(args, rank, world, dist, h):
     abytes = attention_bytes(mine, HEADS, KV_HEADS, HEAD_DIM) * layers
     peak, _, kind = peaks()
     achieved = h.sum_over_ranks(abytes) / world / step_s / 1e9
-    return {"metric": "36-layer decode-step attention tok/s", "workload": "layers36",
+    return {"metric": "36-layer decode-step RoPE+append+attention tok/s", "workload": "layers36",
             "value": h.sum_over_ranks(T) / step_s, "unit": "tok/s", "n_gpus": world,
             "steps": k, "warmup": w, "ms_per_step": ms / k, "tokens_per_gpu_step": T,
             "bytes_per_gpu_step": abytes, "hbm_gbs_per_gpu": achieved,
@@ -613,7 +683,7 @@ def traffic_from_profile():
 
 
 RUNNERS = {"decode64": run_decode64, "mixed": run_mixed, "layers36": run_layers36,
-           "tp2long": run_tp2long}
+           "tp2long": run_tp2long, "rope": run_rope}
 
 
 def main():
