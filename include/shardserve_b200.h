@@ -113,6 +113,30 @@ SS_API int ss_rope_kv_append(const void* q, const int64_t q_strides[3], void* q_
                       int64_t num_pages, void* workspace, void* stream);
 
 /*
+ * Per-step attention metadata built on the device.  Replaces the host loops and copies of
+ * metadata(plan, cache, device, context, bucket) (shardserve/runtime.py:28-49), with the
+ * same output bit for bit.  The caller keeps every live request's block list on the device
+ * (`store`: int32 rows of stride store_row_stride, `store_lens`: blocks per row), written
+ * once when the request is admitted, and passes per step one packed int64 device buffer:
+ *     packed[4 r + 0..3] = store row (-1 for a graph-padding row), query length, first
+ *                          position, offset of the row's first token     (r < rows)
+ *     packed[4 rows + s] = sampled token index s                          (s < n_selected)
+ *     packed[4 rows + n_selected + t] = token id t                        (t < tokens)
+ * Outputs (device): tables int32 [rows, table_cols] (row stride table_row_stride), ids /
+ * positions / slots int64 [tokens], seqs int32 [tokens], selected int64 [n_selected].
+ * Padding rows get tables[r, 0] = pad_block_base + r and one token (id 0, position 0,
+ * slot (pad_block_base + r) * 16), as runtime.py:41-44.  A store row outside the store
+ * (SS_DEVERR_SEQ) or a position outside the request's blocks (SS_DEVERR_POS) yields slot -1.
+ * workspace: optional error word, as ss_kv_append.
+ */
+SS_API int ss_build_metadata(const int64_t* packed, int64_t rows, int64_t n_selected,
+                      int64_t tokens, const int32_t* store, const int32_t* store_lens,
+                      int64_t store_rows, int64_t store_row_stride, int64_t pad_block_base,
+                      int32_t* tables, int64_t table_cols, int64_t table_row_stride,
+                      int64_t* ids, int64_t* positions, int32_t* seqs, int64_t* slots,
+                      int64_t* selected, void* workspace, void* stream);
+
+/*
  * Workspace size (bytes) that ss_ragged_paged_attention needs on `device` for this geometry.
  * Byte 0..3 of the workspace is the device error word (zero it to start clean).  Bytes
  * 64..71 hold the chunked-prefill work counter: they must be zero before the first call (a

@@ -17,8 +17,9 @@ from .kernel import (  # noqa: F401
     rope_kv_append,
 )
 from .cache import Blocks, Cache  # noqa: F401
+from .metadata import DeviceMetadata  # noqa: F401
 
 __all__ = [
     "KernelUnsupported", "SUPPORTED_BLOCK_SIZE", "SUPPORTED_RAGGED_HEAD_DIMS", "kv_append",
-    "ragged_attention_direct", "rope_kv_append", "Blocks", "Cache",
+    "ragged_attention_direct", "rope_kv_append", "Blocks", "Cache", "DeviceMetadata",
 ]

@@ -42,6 +42,10 @@ SIGNATURES = {
         _vp, _i64p, _vp, _i64p, _vp, _i64p, _vp, _i64p, _vp, _i64p, _vp, _i64p, ctypes.c_int64,
         _vp, ctypes.c_int, _vp, _i64p, _vp, _i64p, _vp, ctypes.c_int, ctypes.c_int64,
         ctypes.c_int, ctypes.c_int, ctypes.c_int, ctypes.c_int64, _vp, _vp]),
+    "ss_build_metadata": (ctypes.c_int, [
+        _vp, ctypes.c_int64, ctypes.c_int64, ctypes.c_int64, _vp, _vp, ctypes.c_int64,
+        ctypes.c_int64, ctypes.c_int64, _vp, ctypes.c_int64, ctypes.c_int64, _vp, _vp, _vp, _vp,
+        _vp, _vp, _vp]),
     "ss_attention_workspace_bytes": (ctypes.c_int, [
         ctypes.c_int, ctypes.c_int64, ctypes.c_int, ctypes.c_int, ctypes.c_int,
         ctypes.POINTER(ctypes.c_size_t)]),

@@ -173,6 +173,25 @@ struct RopeArgs {
 };
 cudaError_t launch_rope_append(const RopeArgs& r, bool vectorised, cudaStream_t stream);
 
+// Per-step attention metadata built on the device (metadata.cu).
+struct MetadataArgs {
+  const long long* packed;  // [rows x 4 | n_sel | tokens] int64
+  long long rows, n_sel, tokens;
+  const int* store;         // int32 block lists of live requests, row stride store_rs
+  const int* store_lens;    // blocks held by each store row
+  long long store_rows, store_rs;
+  long long pad_base;       // first graph-padding block (the allocator's block count)
+  int* tables;
+  long long table_cols, table_rs;
+  long long* ids;
+  long long* positions;
+  int* seqs;
+  long long* slots;
+  long long* selected;
+  unsigned* err;            // may be null
+};
+cudaError_t launch_build_metadata(const MetadataArgs& m, cudaStream_t stream);
+
 // Sets the text ss_last_error_message() returns on this thread (printf-style).
 void set_error_message(const char* fmt, ...);
 

@@ -259,6 +259,44 @@ int ss_rope_kv_append(const void* q, const int64_t q_strides[3], void* q_out,
   return SS_OK;
 }
 
+int ss_build_metadata(const int64_t* packed, int64_t rows, int64_t n_selected, int64_t tokens,
+                      const int32_t* store, const int32_t* store_lens, int64_t store_rows,
+                      int64_t store_row_stride, int64_t pad_block_base, int32_t* tables,
+                      int64_t table_cols, int64_t table_row_stride, int64_t* ids,
+                      int64_t* positions, int32_t* seqs, int64_t* slots, int64_t* selected,
+                      void* workspace, void* stream) {
+  if (rows < 0 || n_selected < 0 || tokens < 0 || table_cols < 1 || store_rows < 0)
+    return fail(SS_ERR_INVALID, "negative size or empty table width");
+  if (rows == 0) return SS_OK;
+  if (!packed || !tables || (tokens > 0 && (!ids || !positions || !seqs || !slots)) ||
+      (n_selected > 0 && !selected) || (store_rows > 0 && (!store || !store_lens)))
+    return fail(SS_ERR_INVALID, "null pointer argument");
+  if (table_row_stride < table_cols || (store_rows > 0 && store_row_stride < 1))
+    return fail(SS_ERR_INVALID, "row strides must cover the rows");
+  ss::MetadataArgs m;
+  m.packed = reinterpret_cast<const long long*>(packed);
+  m.rows = rows;
+  m.n_sel = n_selected;
+  m.tokens = tokens;
+  m.store = store;
+  m.store_lens = store_lens;
+  m.store_rows = store_rows;
+  m.store_rs = store_row_stride;
+  m.pad_base = pad_block_base;
+  m.tables = tables;
+  m.table_cols = table_cols;
+  m.table_rs = table_row_stride;
+  m.ids = reinterpret_cast<long long*>(ids);
+  m.positions = reinterpret_cast<long long*>(positions);
+  m.seqs = seqs;
+  m.slots = reinterpret_cast<long long*>(slots);
+  m.selected = reinterpret_cast<long long*>(selected);
+  m.err = workspace ? static_cast<unsigned*>(workspace) : nullptr;
+  const cudaError_t e = ss::launch_build_metadata(m, static_cast<cudaStream_t>(stream));
+  if (e != cudaSuccess) return cuda_fail(e, "build_metadata launch");
+  return SS_OK;
+}
+
 int ss_attention_workspace_bytes(int device, int64_t tokens, int heads, int kv_heads,
                                  int head_dim, size_t* bytes) {
   if (!bytes) return fail(SS_ERR_INVALID, "bytes is null");
