@@ -11,6 +11,9 @@ Other workloads (`--workload`, one JSON line each; same timing rules):
             chunk) + 56 decode rows with context U[256, 4096], one ragged launch per step
   rope      one decode layer's RoPE of q / k + K/V append for the batch-64 workload: the
             fused launch against the same work as separate torch ops
+  metadata  per-step attention metadata (tables, ids, positions, seqs, slots, selected) of
+            the batch-64 decode plan and the mixed plan: the reference's host build against
+            the device-side build (wall clock; host-bound)
   layers36  256 sequences (split over the GPUs) with context U[512, 8192]; one step = the
             36 layers' fused RoPE (theta 1e6) + append and attention, per-layer pools; q/k/v
             come from random-init Qwen2.5-3B projections of N(0,1) hidden states
@@ -60,7 +63,8 @@ def parse():
     p.add_argument("--steps", type=int, default=4000)
     p.add_argument("--warmup", type=int, default=200)
     p.add_argument("--impl", choices=["ours", "reference"], default="ours")
-    p.add_argument("--workload", choices=["decode64", "mixed", "layers36", "tp2long", "rope"],
+    p.add_argument("--workload",
+                   choices=["decode64", "mixed", "layers36", "tp2long", "rope", "metadata"],
                    default="decode64")
     p.add_argument("--replicas", type=int, default=4, help="batches rotated to defeat L2")
     p.add_argument("--graph-steps", type=int, default=100, help="steps per captured graph")
@@ -527,6 +531,93 @@ def run_rope(args, rank, world, dist, h):
             "dtype": "bf16", "data": "synthetic", "scaling": "weak"}
 
 
+def host_metadata(plan, blocks, device, context, bucket=None):
+    """The reference's per-step metadata build (shardserve/runtime.py:28-49): Python loops
+    over tokens, one host-to-device copy per block-table row and per output tensor."""
+    import torch
+
+    rows = plan["rows"]
+    n = bucket or len(rows)
+    tables = torch.zeros((n, (context + 15) // 16), dtype=torch.int32, device=device)
+    tokens, positions, seqs, slots, selected = [], [], [], [], []
+    for i, row in enumerate(rows):
+        table = blocks.tables[row["request_id"]]
+        tables[i, :len(table)] = torch.tensor(table, dtype=torch.int32, device=device)
+        tokens.extend(row["tokens"])
+        positions.extend(row["positions"])
+        seqs.extend([i] * row["query_length"])
+        slots.extend(table[p // 16] * 16 + p % 16 for p in row["positions"])
+        if row["sample"]:
+            selected.append(row["offset"] + row["query_length"] - 1)
+    for i in range(len(rows), n):
+        block = blocks.count + i
+        tables[i, 0] = block
+        tokens.append(0)
+        positions.append(0)
+        seqs.append(i)
+        slots.append(block * 16)
+    return dict(ids=torch.tensor(tokens, dtype=torch.long, device=device),
+                positions=torch.tensor(positions, dtype=torch.long, device=device),
+                tables=tables, seqs=torch.tensor(seqs, dtype=torch.int32, device=device),
+                slots=torch.tensor(slots, dtype=torch.long, device=device),
+                selected=torch.tensor(selected, dtype=torch.long, device=device))
+
+
+def run_metadata(args, rank, world, dist, h):
+    """Per-step attention metadata for the batch-64 decode plan and the mixed plan (56
+    decode rows + 8 x 512-token chunks): the reference's host build against DeviceMetadata.
+    Host-bound, so timed by wall clock around build + synchronize, median of the steps."""
+    import random
+
+    import torch
+
+    from shardserve_b200 import Blocks, DeviceMetadata
+
+    rnd = random.Random(args.seed + rank)
+    context = 4096
+
+    def plan(specs, blocks):
+        rows, offset, caps = [], 0, {}
+        for i, (cursor, n) in enumerate(specs):
+            key = f"r{i}"
+            caps[key] = min(cursor + n + 16, context)
+            rows.append(dict(request_id=key, tokens=[rnd.randint(1, 150000) for _ in range(n)],
+                             context=cursor, positions=list(range(cursor, cursor + n)),
+                             offset=offset, query_length=n, sample=True))
+            offset += n
+        blocks.reserve(caps)
+        return {"rows": rows}
+
+    out = {}
+    for name, specs in (("decode64", [(rnd.randint(127, 4094), 1) for _ in range(BATCH)]),
+                        ("mixed", [(rnd.randint(255, 4094), 1) for _ in range(56)]
+                         + [(rnd.randint(0, 2048), 512) for _ in range(8)])):
+        blocks = Blocks(40000)
+        p = plan(specs, blocks)
+        dm = DeviceMetadata(blocks, h.dev, context)
+        res = {}
+        for label, fn in (("reference_host", lambda: host_metadata(p, blocks, h.dev, context)),
+                          ("device", lambda: dm.build(p))):
+            for _ in range(max(3, args.warmup // 10)):
+                fn()
+            torch.cuda.synchronize()
+            times = []
+            for _ in range(max(20, args.steps // 10)):
+                t0 = time.perf_counter()
+                fn()
+                torch.cuda.synchronize()
+                times.append(time.perf_counter() - t0)
+            res[label + "_us"] = statistics.median(times) * 1e6
+        res["speedup"] = res["reference_host_us"] / res["device_us"]
+        res["tokens"] = sum(n for _, n in specs)
+        out[name] = res
+    return {"metric": "step metadata build us (batch-64 decode plan)", "workload": "metadata",
+            "value": out["decode64"]["device_us"], "unit": "us", "higher_is_better": False,
+            "n_gpus": world, "steps": max(20, args.steps // 10), "plans": out,
+            "timing": "host wall clock around build + synchronize, median",
+            "dtype": "int32/int64", "data": "synthetic plans", "scaling": "weak"}
+
+
 def run_layers36(args, rank, world, dist, h):
     """36 layers of decode attention for 256 sequences (split over the GPUs): q/k/v from
     random-init projections of N(0,1) hidden states; each layer's step rotates q/k with RoPE
@@ -683,7 +774,7 @@ def traffic_from_profile():
 
 
 RUNNERS = {"decode64": run_decode64, "mixed": run_mixed, "layers36": run_layers36,
-           "tp2long": run_tp2long, "rope": run_rope}
+           "tp2long": run_tp2long, "rope": run_rope, "metadata": run_metadata}
 
 
 def main():
