@@ -17,7 +17,7 @@ CSRC = os.path.join(PKG_DIR, "csrc")
 LIB_NAME = "libshardserve_b200.so"
 LIB_PATH = os.path.join(PKG_DIR, LIB_NAME)
 SOURCES = ["capi.cu", "decode_attention.cu", "generic_attention.cu", "kv_append.cu", "noalloc.cu",
-           "prefill_attention.cu", "rope_append.cu", "metadata.cu"]
+           "prefill_attention.cu", "rope_append.cu", "metadata.cu", "tp2_oproj.cu"]
 HEADERS = ["attention.cuh", "ptx.cuh"]
 
 NVCC_FLAGS = [

@@ -192,6 +192,25 @@ struct MetadataArgs {
 };
 cudaError_t launch_build_metadata(const MetadataArgs& m, cudaStream_t stream);
 
+// TP2 o_proj GEMM fused with the two-rank all-reduce (tp2_oproj.cu).
+struct OprojArgs {
+  long long T, T_max;      // tokens of this call, inbox capacity in tokens
+  int N, K;                // output features, per-rank input features
+  __nv_bfloat16* out;      // [T, N], row stride out_rs
+  long long out_rs;
+  const __nv_bfloat16* local_inbox;  // [2][T_max][N]: the peer's partials land here
+  __nv_bfloat16* peer_inbox;         // the peer's inbox (peer memory)
+  const unsigned* local_flags;       // [2][tiles_max]
+  unsigned* peer_flags;
+  int tiles_max;
+  unsigned epoch;          // call number (>= 1); parity selects the inbox / flag half
+  unsigned* err;
+};
+int oproj_tile_features();
+int oproj_tile_tokens();
+cudaError_t launch_tp2_oproj(const CUtensorMap& tmA, const CUtensorMap& tmW, const OprojArgs& o,
+                             cudaStream_t stream);
+
 // Sets the text ss_last_error_message() returns on this thread (printf-style).
 void set_error_message(const char* fmt, ...);
 

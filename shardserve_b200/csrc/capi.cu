@@ -297,6 +297,117 @@ int ss_build_metadata(const int64_t* packed, int64_t rows, int64_t n_selected, i
   return SS_OK;
 }
 
+int ss_device_alloc_zeroed(size_t bytes, void** ptr) {
+  if (!ptr || bytes == 0) return fail(SS_ERR_INVALID, "ptr is null or bytes is zero");
+  cudaError_t e = cudaMalloc(ptr, bytes);
+  if (e == cudaSuccess) e = cudaMemset(*ptr, 0, bytes);
+  if (e != cudaSuccess) return cuda_fail(e, "device allocation");
+  return SS_OK;
+}
+
+int ss_device_free(void* ptr) {
+  const cudaError_t e = cudaFree(ptr);
+  return e == cudaSuccess ? SS_OK : cuda_fail(e, "cudaFree");
+}
+
+int ss_ipc_handle(void* ptr, void* handle64) {
+  if (!ptr || !handle64) return fail(SS_ERR_INVALID, "null pointer argument");
+  cudaIpcMemHandle_t h;
+  const cudaError_t e = cudaIpcGetMemHandle(&h, ptr);
+  if (e != cudaSuccess) return cuda_fail(e, "cudaIpcGetMemHandle");
+  static_assert(sizeof(h) == 64, "IPC handles are 64 bytes");
+  memcpy(handle64, &h, sizeof(h));
+  return SS_OK;
+}
+
+int ss_ipc_open(const void* handle64, void** ptr) {
+  if (!ptr || !handle64) return fail(SS_ERR_INVALID, "null pointer argument");
+  cudaIpcMemHandle_t h;
+  memcpy(&h, handle64, sizeof(h));
+  const cudaError_t e = cudaIpcOpenMemHandle(ptr, h, cudaIpcMemLazyEnablePeerAccess);
+  return e == cudaSuccess ? SS_OK : cuda_fail(e, "cudaIpcOpenMemHandle");
+}
+
+int ss_ipc_close(void* ptr) {
+  const cudaError_t e = cudaIpcCloseMemHandle(ptr);
+  return e == cudaSuccess ? SS_OK : cuda_fail(e, "cudaIpcCloseMemHandle");
+}
+
+namespace {
+// Row-major bf16 matrix [rows, cols] (unit column stride) as a 2-D TMA map whose box is
+// 64 columns (one 128-byte swizzle atom) x box_rows rows.
+bool encode_rows_map(CUtensorMap* map, const void* base, long long rows, long long cols,
+                     long long row_stride, int box_rows) {
+  EncodeTiledFn fn = encode_fn();
+  if (!fn) return false;
+  cuuint64_t dims[2] = {static_cast<cuuint64_t>(cols), static_cast<cuuint64_t>(rows)};
+  cuuint64_t strides[1] = {static_cast<cuuint64_t>(row_stride) * 2};
+  cuuint32_t box[2] = {64, static_cast<cuuint32_t>(box_rows)};
+  cuuint32_t estr[2] = {1, 1};
+  return fn(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(base), dims, strides, box,
+            estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+            CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+}  // namespace
+
+int ss_tp2_oproj_allreduce(const void* attn, const int64_t attn_strides[2], const void* w_o,
+                           const int64_t w_strides[2], void* out, const int64_t out_strides[2],
+                           int64_t tokens, int out_features, int in_features,
+                           const void* local_inbox, void* peer_inbox, const void* local_flags,
+                           void* peer_flags, int64_t max_tokens, int max_tiles, uint32_t epoch,
+                           void* workspace, void* stream) {
+  if (tokens < 0) return fail(SS_ERR_INVALID, "tokens must be >= 0");
+  if (tokens == 0) return SS_OK;
+  if (!attn || !w_o || !out || !local_inbox || !peer_inbox || !local_flags || !peer_flags ||
+      !attn_strides || !w_strides || !out_strides || !workspace)
+    return fail(SS_ERR_INVALID, "null pointer argument");
+  const int tn = ss::oproj_tile_features(), tm = ss::oproj_tile_tokens();
+  if (out_features < tn || out_features % tn || in_features < 64 || in_features % 64)
+    return fail(SS_ERR_INVALID, "out_features must be a multiple of %d and in_features of 64",
+                tn);
+  if (tokens > max_tokens) return fail(SS_ERR_INVALID, "tokens exceed the inbox capacity");
+  if (epoch == 0) return fail(SS_ERR_INVALID, "epoch must be >= 1");
+  const long long tiles = (tokens + tm - 1) / tm * (out_features / tn);
+  if (tiles > max_tiles) return fail(SS_ERR_INVALID, "more tiles than flag slots");
+  int dev = 0, sms = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess ||
+      cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess)
+    return fail(SS_ERR_CUDA, "device query failed");
+  if (tiles > sms)
+    return fail(SS_ERR_INVALID, "%lld tiles exceed one wave of %d SMs (both ranks' tiles must "
+                "be resident together)", tiles, sms);
+  auto ok16 = [](const void* p, const int64_t* st) {
+    return (reinterpret_cast<uintptr_t>(p) & 15) == 0 && st[1] == 1 && st[0] % 8 == 0 && st[0] > 0;
+  };
+  if (attn_strides[0] < in_features || w_strides[0] < in_features ||
+      out_strides[0] < out_features)
+    return fail(SS_ERR_INVALID, "row strides must cover a row");
+  if (!ok16(attn, attn_strides) || !ok16(w_o, w_strides) || !ok16(out, out_strides))
+    return fail(SS_ERR_INVALID, "attn, w_o and out need unit column stride, row strides that "
+                "are multiples of 8 elements and 16-byte aligned bases");
+  CUtensorMap tmA, tmW;
+  if (!encode_rows_map(&tmA, attn, tokens, in_features, attn_strides[0], tm) ||
+      !encode_rows_map(&tmW, w_o, out_features, in_features, w_strides[0], tn))
+    return fail(SS_ERR_INVALID, "tensor map encoding failed");
+  ss::OprojArgs o;
+  o.T = tokens;
+  o.T_max = max_tokens;
+  o.N = out_features;
+  o.K = in_features;
+  o.out = static_cast<__nv_bfloat16*>(out);
+  o.out_rs = out_strides[0];
+  o.local_inbox = static_cast<const __nv_bfloat16*>(local_inbox);
+  o.peer_inbox = static_cast<__nv_bfloat16*>(peer_inbox);
+  o.local_flags = static_cast<const unsigned*>(local_flags);
+  o.peer_flags = static_cast<unsigned*>(peer_flags);
+  o.tiles_max = max_tiles;
+  o.epoch = epoch;
+  o.err = static_cast<unsigned*>(workspace);
+  const cudaError_t e = ss::launch_tp2_oproj(tmA, tmW, o, static_cast<cudaStream_t>(stream));
+  if (e != cudaSuccess) return cuda_fail(e, "tp2_oproj launch");
+  return SS_OK;
+}
+
 int ss_attention_workspace_bytes(int device, int64_t tokens, int heads, int kv_heads,
                                  int head_dim, size_t* bytes) {
   if (!bytes) return fail(SS_ERR_INVALID, "bytes is null");

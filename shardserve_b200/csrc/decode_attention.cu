@@ -9,7 +9,7 @@
 //    the query tokens gives the total U; CTA c owns units [c*chunk, (c+1)*chunk), so every
 //    CTA streams the same number of pages however ragged the contexts are.
 //  * A producer warp gathers pages through the block table and moves each page of K and of
-//    V with ONE 5-D TMA box (128-byte swizzle, no multicast) into a multi-stage ring guarded
+//    V with ONE 5-D TMA box (128-byte swizzle, loaded by this CTA alone) into a multi-stage ring guarded
 //    by mbarriers.  Every byte of K/V is read from HBM once per call: the GROUP query heads
 //    sharing a KV head consume the same shared-memory page.
 //  * Two consumer warps per KV head take alternate pages.  Per page a warp computes

@@ -25,7 +25,7 @@
 // operations of one thread execute in issue order, so S_t(j+1) may be issued right after
 // the P_t.V(j) that reads P_t from the same columns; every other hand-off goes through an
 // mbarrier.  K and V pages come by TMA (one 2 KiB box per page and 64-dim half, 128-byte
-// swizzle, no multicast) through two-stage rings filled by three producer warps, because
+// swizzle, this CTA's own boxes) through two-stage rings filled by three producer warps, because
 // one thread issues its TMA copies one after another.
 //
 // Scheduling: the grid is persistent (one CTA per SM, at most one per work item).  A work

@@ -61,7 +61,7 @@ __device__ __forceinline__ void prefetch_tensormap(const CUtensorMap* map) {
   asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(map)) : "memory");
 }
 // 5-D tiled load of one box into shared memory, completion signalled on `bar` (tx bytes).
-// No multicast: every CTA reads its own tiles of this GPU's memory.
+// Every CTA reads its own tiles of this GPU's memory.
 __device__ __forceinline__ void tma_load_5d(uint32_t dst, const CUtensorMap* map, uint32_t bar,
                                             int c0, int c1, int c2, int c3, int c4,
                                             uint64_t policy) {
@@ -84,7 +84,16 @@ __device__ __forceinline__ uint64_t l2_policy_evict_last() {
   return p;
 }
 
-// 4-D tiled load (no multicast), completion signalled on `bar`.
+// 2-D tiled load into this CTA's shared memory, completion signalled on `bar`.
+__device__ __forceinline__ void tma_load_2d(uint32_t dst, const CUtensorMap* map, uint32_t bar,
+                                            int c0, int c1) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes"
+      " [%0], [%1, {%2, %3}], [%4];" ::"r"(dst),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(c0), "r"(c1), "r"(bar)
+      : "memory");
+}
+// 4-D tiled load into this CTA's shared memory, completion signalled on `bar`.
 __device__ __forceinline__ void tma_load_4d(uint32_t dst, const CUtensorMap* map, uint32_t bar,
                                             int c0, int c1, int c2, int c3) {
   asm volatile(
