@@ -11,6 +11,8 @@ Other workloads (`--workload`, one JSON line each; same timing rules):
             chunk) + 56 decode rows with context U[256, 4096], one ragged launch per step
   rope      one decode layer's RoPE of q / k + K/V append for the batch-64 workload: the
             fused launch against the same work as separate torch ops
+  tp2oproj  (2+ GPUs) TP2 o_proj GEMM + two-rank all-reduce per layer: the fused NVLink
+            kernel against F.linear + NCCL all-reduce, 32 and 256 tokens
   metadata  per-step attention metadata (tables, ids, positions, seqs, slots, selected) of
             the batch-64 decode plan and the mixed plan: the reference's host build against
             the device-side build (wall clock; host-bound)
@@ -64,7 +66,8 @@ def parse():
     p.add_argument("--warmup", type=int, default=200)
     p.add_argument("--impl", choices=["ours", "reference"], default="ours")
     p.add_argument("--workload",
-                   choices=["decode64", "mixed", "layers36", "tp2long", "rope", "metadata"],
+                   choices=["decode64", "mixed", "layers36", "tp2long", "rope", "metadata",
+                            "tp2oproj"],
                    default="decode64")
     p.add_argument("--replicas", type=int, default=4, help="batches rotated to defeat L2")
     p.add_argument("--graph-steps", type=int, default=100, help="steps per captured graph")
@@ -618,6 +621,76 @@ def run_metadata(args, rank, world, dist, h):
             "dtype": "int32/int64", "data": "synthetic plans", "scaling": "weak"}
 
 
+def run_tp2oproj(args, rank, world, dist, h):
+    """TP2 o_proj + all-reduce per layer (Qwen2.5-3B: hidden 2048, 8 heads x 128 per rank)
+    for 32 and 256 tokens per pair: the fused kernel against F.linear + NCCL all-reduce
+    (the reference's composition, model.py:40).  Ranks pair up (0-1, 2-3, ...); both forms
+    are replayed from CUDA graphs of 100 calls and timed with CUDA events, max over ranks."""
+    import torch
+    import torch.nn.functional as F
+
+    from shardserve_b200.tp2 import TP2OprojAllReduce
+
+    if world < 2 or world % 2:
+        return {"metric": "TP2 o_proj + all-reduce us per layer", "workload": "tp2oproj",
+                "unavailable": "needs an even number of GPUs >= 2"}
+    groups = [dist.new_group([2 * p, 2 * p + 1]) for p in range(world // 2)]
+    group = groups[rank // 2]
+    N, K = 2048, 8 * HEAD_DIM
+    op = TP2OprojAllReduce(group, h.dev, 256, N, K)
+    res = {}
+    for T in (32, 256):
+        g = torch.Generator(device="cpu").manual_seed(args.seed + rank)
+        a = torch.randn(T, K, generator=g).to(torch.bfloat16).to(h.dev)
+        w = (torch.randn(N, K, generator=g) * K ** -0.5).to(torch.bfloat16).to(h.dev)
+        out = torch.empty(T, N, dtype=torch.bfloat16, device=h.dev)
+
+        def fused():
+            op(a, w, out=out)
+
+        def unfused():
+            y = F.linear(a, w)
+            dist.all_reduce(y, group=group)
+
+        for label, fn in (("fused_us", fused), ("linear_nccl_us", unfused)):
+            fn()
+            h.barrier()
+            n_in = min(100, args.steps)
+            stream = torch.cuda.Stream(h.dev)
+            stream.wait_stream(torch.cuda.current_stream(h.dev))
+            graph = torch.cuda.CUDAGraph()
+            with torch.cuda.stream(stream):
+                with torch.cuda.graph(graph, stream=stream):
+                    for _ in range(n_in):
+                        fn()
+            torch.cuda.current_stream(h.dev).wait_stream(stream)
+            reps = max(1, args.steps // n_in)
+            for _ in range(max(1, args.warmup // n_in)):
+                graph.replay()
+            h.barrier()
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record()
+            for _ in range(reps):
+                graph.replay()
+            e1.record()
+            torch.cuda.synchronize()
+            h.barrier()
+            res[f"T{T}_{label}"] = h.max_over_ranks(e0.elapsed_time(e1) * 1e3 / (reps * n_in))
+            del graph  # graphs holding NCCL calls go before the process group does
+        res[f"T{T}_speedup"] = res[f"T{T}_linear_nccl_us"] / res[f"T{T}_fused_us"]
+    err = op.device_errors()
+    op.close()
+    wbytes = N * K * 2
+    peak, _, kind = peaks()
+    return {"metric": "TP2 o_proj + all-reduce us per layer (32 tokens)", "workload": "tp2oproj",
+            "value": res["T32_fused_us"], "unit": "us", "higher_is_better": False,
+            "n_gpus": world, "steps": args.steps, "warmup": args.warmup, **res,
+            "weight_bytes_per_rank": wbytes,
+            "hbm_frac_T32": wbytes / (res["T32_fused_us"] * 1e-6) / 1e9 / peak,
+            "device_errors": err, "peak_kind": kind, "dtype": "bf16", "data": "synthetic",
+            "scaling": "weak", "timing": "graph-replayed calls, CUDA events, max over ranks"}
+
+
 def run_layers36(args, rank, world, dist, h):
     """36 layers of decode attention for 256 sequences (split over the GPUs): q/k/v from
     random-init projections of N(0,1) hidden states; each layer's step rotates q/k with RoPE
@@ -774,7 +847,8 @@ def traffic_from_profile():
 
 
 RUNNERS = {"decode64": run_decode64, "mixed": run_mixed, "layers36": run_layers36,
-           "tp2long": run_tp2long, "rope": run_rope, "metadata": run_metadata}
+           "tp2long": run_tp2long, "rope": run_rope, "metadata": run_metadata,
+           "tp2oproj": run_tp2oproj}
 
 
 def main():

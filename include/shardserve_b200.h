@@ -141,25 +141,28 @@ SS_API int ss_build_metadata(const int64_t* packed, int64_t rows, int64_t n_sele
  * Replaces, per layer and rank, reduce(F.linear(attention, w_o)) of shardserve/model.py:40
  * with reduce = the two-rank all-reduce of shardserve/runtime.py:17-24:
  *     out = bf16(P_0 + P_1),  P_r = bf16(attn_r w_o,r^T)  (fp32 accumulation, as F.linear)
- * Both ranks call it with the same epoch (1, 2, 3, ... per call) and both receive `out`.
+ * Both ranks make the same sequence of calls and both receive `out`.
  * attn        : bf16 [tokens, in_features] (this rank's heads), unit column stride
  * w_o         : bf16 [out_features, in_features] (this rank's column shard of o_proj)
  * out         : bf16 [tokens, out_features]
- * local_inbox / peer_inbox: bf16 [2][max_tokens][out_features] on this rank / the other rank
- *               (the other rank's buffer opened with ss_ipc_open); local_flags / peer_flags:
- *               uint32 [2][max_tiles], likewise.  All four start zeroed
- *               (ss_device_alloc_zeroed) and are never cleared again.
- * Tiles are 128 tokens x 32 features; all tiles of one call must fit one wave of the GPU
- * (tiles <= SM count).  workspace: the 4-byte error word (a partner that does not arrive
- * within ~1 s sets SS_DEVERR_TIMEOUT instead of hanging).  Calls on one rank are
- * stream-ordered; the two ranks' calls with the same epoch run concurrently.
+ * local_inbox / peer_inbox: 8 * max_tokens * out_features bytes on this rank / the other
+ *               rank (its buffer opened with ss_ipc_open), zeroed once
+ *               (ss_device_alloc_zeroed) and never cleared again
+ * epoch_counter: 8 zeroed device bytes per rank that count its calls (the kernel advances
+ *               them, so calls can be replayed from a CUDA graph)
+ * out_features a multiple of 128, in_features of 256.  Tiles are 128 tokens x 32-128
+ * features (wider for more tokens); all tiles of a call must fit one wave of the GPU
+ * (tiles <= SM count).  workspace: the
+ * 4-byte error word (a partner that does not arrive within ~1 s sets SS_DEVERR_TIMEOUT
+ * instead of hanging).  Calls on one rank are stream-ordered; the two ranks' n-th calls
+ * run concurrently.
  */
 SS_API int ss_tp2_oproj_allreduce(const void* attn, const int64_t attn_strides[2],
                            const void* w_o, const int64_t w_strides[2], void* out,
                            const int64_t out_strides[2], int64_t tokens, int out_features,
                            int in_features, const void* local_inbox, void* peer_inbox,
-                           const void* local_flags, void* peer_flags, int64_t max_tokens,
-                           int max_tiles, uint32_t epoch, void* workspace, void* stream);
+                           int64_t max_tokens, void* epoch_counter, void* workspace,
+                           void* stream);
 
 /* Zero-filled device allocation / release (inboxes and flags of ss_tp2_oproj_allreduce). */
 SS_API int ss_device_alloc_zeroed(size_t bytes, void** ptr);

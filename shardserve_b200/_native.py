@@ -48,7 +48,7 @@ SIGNATURES = {
         _vp, _vp, _vp]),
     "ss_tp2_oproj_allreduce": (ctypes.c_int, [
         _vp, _i64p, _vp, _i64p, _vp, _i64p, ctypes.c_int64, ctypes.c_int, ctypes.c_int,
-        _vp, _vp, _vp, _vp, ctypes.c_int64, ctypes.c_int, ctypes.c_uint32, _vp, _vp]),
+        _vp, _vp, ctypes.c_int64, _vp, _vp, _vp]),
     "ss_device_alloc_zeroed": (ctypes.c_int, [ctypes.c_size_t, ctypes.POINTER(ctypes.c_void_p)]),
     "ss_device_free": (ctypes.c_int, [_vp]),
     "ss_ipc_handle": (ctypes.c_int, [_vp, _vp]),

@@ -198,16 +198,19 @@ struct OprojArgs {
   int N, K;                // output features, per-rank input features
   __nv_bfloat16* out;      // [T, N], row stride out_rs
   long long out_rs;
-  const __nv_bfloat16* local_inbox;  // [2][T_max][N]: the peer's partials land here
-  __nv_bfloat16* peer_inbox;         // the peer's inbox (peer memory)
-  const unsigned* local_flags;       // [2][tiles_max]
-  unsigned* peer_flags;
-  int tiles_max;
-  unsigned epoch;          // call number (>= 1); parity selects the inbox / flag half
+  const void* local_inbox; // [2][T_max][N / 2] 8-byte words {bf16 pair, epoch}
+  void* peer_inbox;        // the other rank's inbox (peer memory)
+  int a_rows;              // rows of the attention box actually loaded (<= 128)
+  int tile_n;              // output features per CTA (oproj_tile_n)
+  int atoms;               // 64-column K atoms per ring stage
+  int stages;              // depth of the A/W ring (oproj_ring)
+  unsigned* epoch_ctr;     // [0] last completed call number, [1] CTAs finished (device)
   unsigned* err;
 };
-int oproj_tile_features();
 int oproj_tile_tokens();
+int oproj_min_k_step();
+int oproj_tile_n(long long tokens);
+void oproj_ring(int a_rows, int tn, int k, int* atoms, int* stages);
 cudaError_t launch_tp2_oproj(const CUtensorMap& tmA, const CUtensorMap& tmW, const OprojArgs& o,
                              cudaStream_t stream);
 

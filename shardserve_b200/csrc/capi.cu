@@ -334,17 +334,18 @@ int ss_ipc_close(void* ptr) {
 }
 
 namespace {
-// Row-major bf16 matrix [rows, cols] (unit column stride) as a 2-D TMA map whose box is
-// 64 columns (one 128-byte swizzle atom) x box_rows rows.
+// Row-major bf16 matrix [rows, cols] (unit column stride) as a 3-D TMA map (64 columns,
+// rows, column atoms of 64) whose box is box_rows rows x `atoms` atoms: shared memory gets
+// [atom][row][128 B] with the 128-byte swizzle.
 bool encode_rows_map(CUtensorMap* map, const void* base, long long rows, long long cols,
-                     long long row_stride, int box_rows) {
+                     long long row_stride, int box_rows, int atoms) {
   EncodeTiledFn fn = encode_fn();
   if (!fn) return false;
-  cuuint64_t dims[2] = {static_cast<cuuint64_t>(cols), static_cast<cuuint64_t>(rows)};
-  cuuint64_t strides[1] = {static_cast<cuuint64_t>(row_stride) * 2};
-  cuuint32_t box[2] = {64, static_cast<cuuint32_t>(box_rows)};
-  cuuint32_t estr[2] = {1, 1};
-  return fn(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(base), dims, strides, box,
+  cuuint64_t dims[3] = {64, static_cast<cuuint64_t>(rows), static_cast<cuuint64_t>(cols / 64)};
+  cuuint64_t strides[2] = {static_cast<cuuint64_t>(row_stride) * 2, 128};
+  cuuint32_t box[3] = {64, static_cast<cuuint32_t>(box_rows), static_cast<cuuint32_t>(atoms)};
+  cuuint32_t estr[3] = {1, 1, 1};
+  return fn(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, const_cast<void*>(base), dims, strides, box,
             estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
             CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
@@ -353,22 +354,21 @@ bool encode_rows_map(CUtensorMap* map, const void* base, long long rows, long lo
 int ss_tp2_oproj_allreduce(const void* attn, const int64_t attn_strides[2], const void* w_o,
                            const int64_t w_strides[2], void* out, const int64_t out_strides[2],
                            int64_t tokens, int out_features, int in_features,
-                           const void* local_inbox, void* peer_inbox, const void* local_flags,
-                           void* peer_flags, int64_t max_tokens, int max_tiles, uint32_t epoch,
-                           void* workspace, void* stream) {
+                           const void* local_inbox, void* peer_inbox, int64_t max_tokens,
+                           void* epoch_counter, void* workspace, void* stream) {
   if (tokens < 0) return fail(SS_ERR_INVALID, "tokens must be >= 0");
   if (tokens == 0) return SS_OK;
-  if (!attn || !w_o || !out || !local_inbox || !peer_inbox || !local_flags || !peer_flags ||
-      !attn_strides || !w_strides || !out_strides || !workspace)
+  if (!attn || !w_o || !out || !local_inbox || !peer_inbox || !attn_strides || !w_strides ||
+      !out_strides || !workspace || !epoch_counter)
     return fail(SS_ERR_INVALID, "null pointer argument");
-  const int tn = ss::oproj_tile_features(), tm = ss::oproj_tile_tokens();
-  if (out_features < tn || out_features % tn || in_features < 64 || in_features % 64)
-    return fail(SS_ERR_INVALID, "out_features must be a multiple of %d and in_features of 64",
-                tn);
+  const int tn = ss::oproj_tile_n(tokens), tm = ss::oproj_tile_tokens();
+  const int ks = ss::oproj_min_k_step();
+  if (out_features < 128 || out_features % 128 || in_features < 4 * ks / 2 ||
+      in_features % (2 * ks))
+    return fail(SS_ERR_INVALID, "out_features must be a multiple of 128 and in_features of %d",
+                2 * ks);
   if (tokens > max_tokens) return fail(SS_ERR_INVALID, "tokens exceed the inbox capacity");
-  if (epoch == 0) return fail(SS_ERR_INVALID, "epoch must be >= 1");
   const long long tiles = (tokens + tm - 1) / tm * (out_features / tn);
-  if (tiles > max_tiles) return fail(SS_ERR_INVALID, "more tiles than flag slots");
   int dev = 0, sms = 0;
   if (cudaGetDevice(&dev) != cudaSuccess ||
       cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess)
@@ -376,18 +376,23 @@ int ss_tp2_oproj_allreduce(const void* attn, const int64_t attn_strides[2], cons
   if (tiles > sms)
     return fail(SS_ERR_INVALID, "%lld tiles exceed one wave of %d SMs (both ranks' tiles must "
                 "be resident together)", tiles, sms);
-  auto ok16 = [](const void* p, const int64_t* st) {
-    return (reinterpret_cast<uintptr_t>(p) & 15) == 0 && st[1] == 1 && st[0] % 8 == 0 && st[0] > 0;
-  };
   if (attn_strides[0] < in_features || w_strides[0] < in_features ||
       out_strides[0] < out_features)
     return fail(SS_ERR_INVALID, "row strides must cover a row");
+  auto ok16 = [](const void* p, const int64_t* st) {
+    return (reinterpret_cast<uintptr_t>(p) & 15) == 0 && st[1] == 1 && st[0] % 8 == 0 && st[0] > 0;
+  };
   if (!ok16(attn, attn_strides) || !ok16(w_o, w_strides) || !ok16(out, out_strides))
     return fail(SS_ERR_INVALID, "attn, w_o and out need unit column stride, row strides that "
                 "are multiples of 8 elements and 16-byte aligned bases");
+  // Rows of the attention tile actually loaded: all 128 MMA rows only when the call has
+  // them; rows past it hold stale shared memory and give output rows that are never stored.
+  const int a_rows = static_cast<int>(tokens >= tm ? tm : (tokens + 7) / 8 * 8);
+  int atoms = 0, stages = 0;
+  ss::oproj_ring(a_rows, tn, in_features, &atoms, &stages);
   CUtensorMap tmA, tmW;
-  if (!encode_rows_map(&tmA, attn, tokens, in_features, attn_strides[0], tm) ||
-      !encode_rows_map(&tmW, w_o, out_features, in_features, w_strides[0], tn))
+  if (!encode_rows_map(&tmA, attn, tokens, in_features, attn_strides[0], a_rows, atoms) ||
+      !encode_rows_map(&tmW, w_o, out_features, in_features, w_strides[0], tn, atoms))
     return fail(SS_ERR_INVALID, "tensor map encoding failed");
   ss::OprojArgs o;
   o.T = tokens;
@@ -396,12 +401,13 @@ int ss_tp2_oproj_allreduce(const void* attn, const int64_t attn_strides[2], cons
   o.K = in_features;
   o.out = static_cast<__nv_bfloat16*>(out);
   o.out_rs = out_strides[0];
-  o.local_inbox = static_cast<const __nv_bfloat16*>(local_inbox);
-  o.peer_inbox = static_cast<__nv_bfloat16*>(peer_inbox);
-  o.local_flags = static_cast<const unsigned*>(local_flags);
-  o.peer_flags = static_cast<unsigned*>(peer_flags);
-  o.tiles_max = max_tiles;
-  o.epoch = epoch;
+  o.local_inbox = local_inbox;
+  o.peer_inbox = peer_inbox;
+  o.a_rows = a_rows;
+  o.tile_n = tn;
+  o.atoms = atoms;
+  o.stages = stages;
+  o.epoch_ctr = static_cast<unsigned*>(epoch_counter);
   o.err = static_cast<unsigned*>(workspace);
   const cudaError_t e = ss::launch_tp2_oproj(tmA, tmW, o, static_cast<cudaStream_t>(stream));
   if (e != cudaSuccess) return cuda_fail(e, "tp2_oproj launch");

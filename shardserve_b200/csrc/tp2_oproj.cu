@@ -8,18 +8,22 @@
 // o_proj.  Every rank computes the same out (the sum of two bf16 values is formed in fp32,
 // so both ranks round the same number).
 //
-// One CTA = 128 tokens x 32 output features, full K.  Warp 0 (one thread) loads A and W
-// tiles by TMA (128-byte swizzle, 4-stage ring; local memory only), warp 1 (one thread)
-// issues tcgen05.mma M128 N32 K16 into 32 TMEM columns, then all four warps read their
-// 32-token TMEM quadrant, round P_r to bf16 and store it straight into the PEER's inbox
-// (plain 16-byte stores over NVLink), publish a flag in the peer's memory (release,
-// system scope), wait (bounded) for the peer's flag for the same tile, and add the peer's
-// partial from the local inbox.  The inbox and flags alternate between two halves by call
-// parity and flags carry the call's epoch, so nothing is ever cleared and a rank cannot
-// overwrite a partial the other rank has not consumed.  A CTA never waits for another CTA
-// of its own GPU; it waits only for its counterpart on the other GPU, which stores its
-// partial before it waits.  The grid is at most one wave, so both counterparts are
-// resident.  TMA reads only this GPU's memory; no library kernel touches peer memory.
+// One CTA = 128 tokens x 32 output features (the kernel also takes 64 or 128), full K.
+// Warp 0 (one thread) loads A and W by TMA with 3-D boxes that each carry two or four
+// 64-column K chunks (128-byte swizzle), so a call with K = 1024 needs 8-16 copies per CTA;
+// warp 1 (one thread) issues tcgen05.mma M128 N(tile) K16 into TMEM.  All four warps then
+// read their 32-token TMEM quadrant 32 features at a time and round P_r to bf16.  The
+// exchange uses flag-carrying words: every 8-byte word holds two bf16 partials and the
+// call's epoch, stored with 16-byte volatile stores straight into the
+// other rank's inbox over NVLink; the other rank polls its own inbox words until their
+// epoch is the current one (bounded), so no fence or separate flag is needed, and adds
+// them to its own partial.  Inbox halves alternate by call parity, so a rank never
+// overwrites words the other rank has not read.  The epoch lives in device memory: every
+// CTA reads the last completed call number at its start and the last CTA to finish
+// advances it, so calls can be replayed from a CUDA graph.  A CTA waits only for its
+// counterpart on the other GPU, which writes before it waits; the grid is at most one wave,
+// so both are resident.  TMA reads only this GPU's memory; no library kernel touches peer
+// memory.
 #include <cuda_bf16.h>
 
 #include "attention.cuh"
@@ -29,21 +33,24 @@ namespace ss {
 
 namespace {
 
-constexpr int kTM = 128;   // tokens per tile (MMA M)
-constexpr int kTN = 32;    // features per tile (MMA N)
-constexpr int kTK = 64;    // K per stage (one 128-byte swizzle atom of bf16)
-constexpr int kStagesO = 4;
-constexpr int kABytes = kTM * kTK * 2;  // 16 KiB
-constexpr int kWBytes = kTN * kTK * 2;  // 4 KiB
-constexpr int kStageBytes = kABytes + kWBytes;
-constexpr int kSmemO = kStagesO * kStageBytes + 256 + 1024;
+constexpr int kTM = 128;    // tokens per tile (MMA M)
+constexpr int kTNMax = 128; // features per tile (MMA N): 32, 64 or 128 by call size
+constexpr int kTK = 64;     // K columns per swizzle atom
+constexpr int kMaxStagesO = 8;
+constexpr int kRingBytes = 200 * 1024;
+constexpr int kSmemO = kRingBytes + 512 + 1024;
 
-__device__ __forceinline__ void st_release_sys(unsigned* p, unsigned v) {
-  asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+__device__ __forceinline__ void st_volatile_v4(void* p, uint4 v) {
+  asm volatile("st.volatile.global.v4.u32 [%0], {%1, %2, %3, %4};" ::"l"(p), "r"(v.x), "r"(v.y),
+               "r"(v.z), "r"(v.w)
+               : "memory");
 }
-__device__ __forceinline__ unsigned ld_acquire_sys(const unsigned* p) {
-  unsigned v;
-  asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+__device__ __forceinline__ uint4 ld_volatile_v4(const void* p) {
+  uint4 v;
+  asm volatile("ld.volatile.global.v4.u32 {%0, %1, %2, %3}, [%4];"
+               : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w)
+               : "l"(p)
+               : "memory");
   return v;
 }
 
@@ -54,18 +61,23 @@ __global__ void __launch_bounds__(128, 1)
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
                                              ~static_cast<uintptr_t>(1023));
   const uint32_t sb = smem_u32(smem);
-  const uint32_t bars = sb + kStagesO * kStageBytes;  // full[4], empty[4], done
+  const int nst = o.stages, kc = o.atoms, tn = o.tile_n;
+  const int a_chunk = o.a_rows * kTK * 2;              // one 64-column atom of A rows
+  const int w_chunk = tn * kTK * 2;
+  const int a_stage = kc * a_chunk, stage_bytes = a_stage + kc * w_chunk;
+  const uint32_t bars = sb + kRingBytes;               // full[8], empty[8], done
   auto full = [&](int s) { return bars + 8 * s; };
-  auto empty = [&](int s) { return bars + 8 * (kStagesO + s); };
-  const uint32_t done = bars + 8 * (2 * kStagesO);
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + kStagesO * kStageBytes + 128);
+  auto empty = [&](int s) { return bars + 8 * (kMaxStagesO + s); };
+  const uint32_t done = bars + 8 * (2 * kMaxStagesO);
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + kRingBytes + 320);
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-  const int n0 = blockIdx.x * kTN;
+  const int n0 = blockIdx.x * tn;
   const long long m0 = static_cast<long long>(blockIdx.y) * kTM;
-  const int kblocks = o.K / kTK;
+  const int nload = o.K / (kTK * kc);                  // ring stages of this call
+  const unsigned epoch = *reinterpret_cast<volatile const unsigned*>(o.epoch_ctr) + 1u;
 
   if (tid == 0) {
-    for (int s = 0; s < kStagesO; ++s) {
+    for (int s = 0; s < nst; ++s) {
       mbar_init(full(s), 1);
       mbar_init(empty(s), 1);
     }
@@ -73,7 +85,7 @@ __global__ void __launch_bounds__(128, 1)
     fence_mbar_init();
   }
   if (warp == 0) {
-    tmem_alloc(smem_u32(tmem_slot), 32);
+    tmem_alloc(smem_u32(tmem_slot), kTNMax);
     tmem_relinquish();
   }
   tc_fence_before();
@@ -82,30 +94,32 @@ __global__ void __launch_bounds__(128, 1)
   const uint32_t tmem = *tmem_slot;
   bool ok = true;
 
-  if (warp == 0 && lane == 0) {  // ---- TMA producer
+  if (warp == 0 && lane == 0) {  // ---- TMA producer: 3-D boxes of kc atoms
     prefetch_tensormap(&tmA);
     prefetch_tensormap(&tmW);
-    for (int kb = 0; kb < kblocks && ok; ++kb) {
-      const int s = kb % kStagesO;
-      ok = mbar_wait(empty(s), ((kb / kStagesO) & 1) ^ 1);
+    for (int i = 0; i < nload && ok; ++i) {
+      const int s = i % nst;
+      ok = mbar_wait(empty(s), ((i / nst) & 1) ^ 1);
       if (!ok) break;
-      const uint32_t dst = sb + s * kStageBytes;
-      mbar_arrive_expect_tx(full(s), kStageBytes);
-      tma_load_2d(dst, &tmA, full(s), kb * kTK, static_cast<int>(m0));
-      tma_load_2d(dst + kABytes, &tmW, full(s), kb * kTK, n0);
+      const uint32_t dst = sb + s * stage_bytes;
+      mbar_arrive_expect_tx(full(s), stage_bytes);
+      tma_load_3d(dst, &tmA, full(s), 0, static_cast<int>(m0), i * kc);
+      tma_load_3d(dst + a_stage, &tmW, full(s), 0, n0, i * kc);
     }
   } else if (warp == 1 && lane == 0) {  // ---- MMA issuer
-    constexpr uint32_t idesc = idesc_bf16_f32(kTM, kTN, 0, 0);
-    for (int kb = 0; kb < kblocks && ok; ++kb) {
-      const int s = kb % kStagesO;
-      ok = mbar_wait(full(s), (kb / kStagesO) & 1);
+    const uint32_t idesc = idesc_bf16_f32(kTM, tn, 0, 0);
+    for (int i = 0; i < nload && ok; ++i) {
+      const int s = i % nst;
+      ok = mbar_wait(full(s), (i / nst) & 1);
       if (!ok) break;
       tc_fence_after();
-      const uint32_t a = sb + s * kStageBytes, w = a + kABytes;
+      const uint32_t a = sb + s * stage_bytes, w = a + a_stage;
+      for (int c = 0; c < kc; ++c)
 #pragma unroll
-      for (int kk = 0; kk < kTK / 16; ++kk)
-        tc_mma_f16(tmem, smem_desc_sw128(a + kk * 32, 16, 1024),
-                   smem_desc_sw128(w + kk * 32, 16, 1024), idesc, (kb > 0 || kk > 0) ? 1u : 0u);
+        for (int kk = 0; kk < kTK / 16; ++kk)
+          tc_mma_f16(tmem, smem_desc_sw128(a + c * a_chunk + kk * 32, 16, 1024),
+                     smem_desc_sw128(w + c * w_chunk + kk * 32, 16, 1024), idesc,
+                     (i > 0 || c > 0 || kk > 0) ? 1u : 0u);
       tc_commit(empty(s));
     }
     tc_commit(done);
@@ -113,78 +127,110 @@ __global__ void __launch_bounds__(128, 1)
   __syncwarp();
   if (!ok) atomicOr(o.err, SS_DEVERR_TIMEOUT);
 
-  // ---- epilogue: every warp owns 32 tokens (its TMEM lane quadrant) x 32 features
+  // ---- epilogue: every warp owns 32 tokens (its TMEM lane quadrant); groups of 32
+  // features are rounded, exchanged and summed one after another.
   const bool mma_ok = __all_sync(0xffffffffu, mbar_wait(done, 0));
-  const int parity = static_cast<int>(o.epoch & 1u);
   const long long row = m0 + (warp & 3) * 32 + lane;
   const bool live = mma_ok && row < o.T;
-  uint32_t acc[32];
-  if (mma_ok) {
-    tc_fence_after();
-    tmem_ld32(tmem + (static_cast<uint32_t>((warp & 3) * 32) << 16), acc);
-    tmem_wait_ld();
-  }
-  float mine[32];
-  uint32_t packed[16];
+  if (mma_ok) tc_fence_after();
+  bool timed_out = false;
+  for (int g = 0; g < tn / 32; ++g) {
+    const int f0 = n0 + 32 * g;
+    uint32_t acc[32];
+    if (mma_ok) {
+      tmem_ld32(tmem + (static_cast<uint32_t>((warp & 3) * 32) << 16) + 32 * g, acc);
+      tmem_wait_ld();
+    }
+    uint32_t pk[16];  // this rank's partial: bf16 pairs (features 2i, 2i + 1)
 #pragma unroll
-  for (int i = 0; i < 32; i += 2) {
-    const __nv_bfloat162 p = __floats2bfloat162_rn(__uint_as_float(acc[i]), __uint_as_float(acc[i + 1]));
-    packed[i / 2] = *reinterpret_cast<const uint32_t*>(&p);
-    mine[i] = __low2float(p);
-    mine[i + 1] = __high2float(p);
-  }
-  const long long inbox_off = (static_cast<long long>(parity) * o.T_max + row) * o.N + n0;
-  if (live) {  // this rank's partial into the peer's inbox (16-byte stores over NVLink)
-    uint4* dst = reinterpret_cast<uint4*>(o.peer_inbox + inbox_off);
+    for (int i = 0; i < 16; ++i) {
+      const __nv_bfloat162 p = __floats2bfloat162_rn(__uint_as_float(acc[2 * i]),
+                                                     __uint_as_float(acc[2 * i + 1]));
+      pk[i] = *reinterpret_cast<const uint32_t*>(&p);
+    }
+    // Inbox word (token, feature pair) = {bf16 pair, epoch}; 16 words per thread and group.
+    const long long word0 = ((static_cast<long long>(epoch & 1u) * o.T_max + row) * o.N + f0) / 2;
+    if (live) {
+      uint2* dst = reinterpret_cast<uint2*>(o.peer_inbox) + word0;
 #pragma unroll
-    for (int q = 0; q < 4; ++q)
-      dst[q] = make_uint4(packed[4 * q], packed[4 * q + 1], packed[4 * q + 2], packed[4 * q + 3]);
-  }
-  __syncthreads();
-  const int tile = blockIdx.y * gridDim.x + blockIdx.x;
-  if (tid == 0) {
-    __threadfence_system();
-    st_release_sys(o.peer_flags + parity * o.tiles_max + tile, o.epoch);
-    // Wait (bounded) for the other rank's partial of this tile in the local inbox.
-    const unsigned* f = o.local_flags + parity * o.tiles_max + tile;
-    const long long start = clock64();
-    bool arrived = ld_acquire_sys(f) == o.epoch;
-    while (!arrived && clock64() - start < kWaitLimitCycles) arrived = ld_acquire_sys(f) == o.epoch;
-    if (!arrived) atomicOr(o.err, SS_DEVERR_TIMEOUT);
-    *reinterpret_cast<volatile int*>(smem + kStagesO * kStageBytes + 132) = arrived ? 1 : 0;
-  }
-  __syncthreads();
-  const bool arrived = *reinterpret_cast<volatile int*>(smem + kStagesO * kStageBytes + 132) != 0;
-  if (live && arrived) {
-    const uint4* src = reinterpret_cast<const uint4*>(o.local_inbox + inbox_off);
-    __nv_bfloat16* out = o.out + row * o.out_rs + n0;
+      for (int q = 0; q < 8; ++q)
+        st_volatile_v4(dst + 2 * q, make_uint4(pk[2 * q], epoch, pk[2 * q + 1], epoch));
+    }
+    if (live && !timed_out) {  // the other rank's partial: poll until every word is current
+      const uint2* src = reinterpret_cast<const uint2*>(o.local_inbox) + word0;
+      uint32_t theirs[16];
+      unsigned pending = 0xFFu;  // one bit per 16-byte pair of words
+      const long long start = clock64();
+      while (pending) {
 #pragma unroll
-    for (int q = 0; q < 4; ++q) {
-      const uint4 v = __ldcv(src + q);  // the peer wrote it: bypass L1
-      const uint32_t w[4] = {v.x, v.y, v.z, v.w};
-      uint32_t r[4];
-#pragma unroll
-      for (int e = 0; e < 4; ++e) {
-        const float lo = __uint_as_float(w[e] << 16), hi = __uint_as_float(w[e] & 0xFFFF0000u);
-        const __nv_bfloat162 s = __floats2bfloat162_rn(__fadd_rn(mine[8 * q + 2 * e], lo),
-                                                       __fadd_rn(mine[8 * q + 2 * e + 1], hi));
-        r[e] = *reinterpret_cast<const uint32_t*>(&s);
+        for (int q = 0; q < 8; ++q) {
+          if (pending & (1u << q)) {
+            const uint4 v = ld_volatile_v4(src + 2 * q);
+            if (v.y == epoch && v.w == epoch) {
+              theirs[2 * q] = v.x;
+              theirs[2 * q + 1] = v.z;
+              pending &= ~(1u << q);
+            }
+          }
+        }
+        if (pending && clock64() - start > kWaitLimitCycles) break;
       }
-      reinterpret_cast<uint4*>(out)[q] = make_uint4(r[0], r[1], r[2], r[3]);
+      if (pending) {
+        atomicOr(o.err, SS_DEVERR_TIMEOUT);
+        timed_out = true;
+      } else {
+        uint32_t r[16];
+#pragma unroll
+        for (int i = 0; i < 16; ++i) {
+          const float a0 = __uint_as_float(pk[i] << 16), a1 = __uint_as_float(pk[i] & 0xFFFF0000u);
+          const float b0 = __uint_as_float(theirs[i] << 16);
+          const float b1 = __uint_as_float(theirs[i] & 0xFFFF0000u);
+          const __nv_bfloat162 s2 = __floats2bfloat162_rn(__fadd_rn(a0, b0), __fadd_rn(a1, b1));
+          r[i] = *reinterpret_cast<const uint32_t*>(&s2);
+        }
+        uint4* out = reinterpret_cast<uint4*>(o.out + row * o.out_rs + f0);
+#pragma unroll
+        for (int q = 0; q < 4; ++q)
+          out[q] = make_uint4(r[4 * q], r[4 * q + 1], r[4 * q + 2], r[4 * q + 3]);
+      }
     }
   }
   tc_fence_before();
   __syncthreads();
   if (warp == 0) {
     tc_fence_after();
-    tmem_dealloc(tmem, 32);
+    tmem_dealloc(tmem, kTNMax);
+  }
+  if (tid == 0) {  // the last CTA out records this call as complete
+    __threadfence();
+    if (atomicAdd(o.epoch_ctr + 1, 1u) == gridDim.x * gridDim.y - 1) {
+      atomicExch(o.epoch_ctr, epoch);
+      atomicExch(o.epoch_ctr + 1, 0u);
+    }
   }
 }
 
 }  // namespace
 
-int oproj_tile_features() { return kTN; }
 int oproj_tile_tokens() { return kTM; }
+int oproj_min_k_step() { return kTK * 2; }
+// Features per tile.  The kernel handles 32, 64 and 128; 32 measured fastest at 32 and 256
+// tokens per pair (more CTAs share the loads of W; wider tiles halve the re-reads of A but
+// leave too few CTAs issuing copies).
+int oproj_tile_n(long long) { return 32; }
+// Atoms per stage and ring depth: the largest stage (4, then 2 atoms) that still leaves two
+// stages in the ring, and as many stages as fit (at most one per load).
+void oproj_ring(int a_rows, int tn, int k, int* atoms, int* stages) {
+  int kc = 4;
+  while (kc > 2 && 2 * kc * (a_rows + tn) * kTK * 2 > kRingBytes) kc /= 2;
+  if ((k / kTK) % kc) kc = 2;
+  const int stage = kc * (a_rows + tn) * kTK * 2;
+  int n = kRingBytes / stage;
+  if (n > kMaxStagesO) n = kMaxStagesO;
+  const int loads = k / (kTK * kc);
+  *atoms = kc;
+  *stages = n < loads ? n : loads;
+}
 
 cudaError_t launch_tp2_oproj(const CUtensorMap& tmA, const CUtensorMap& tmW, const OprojArgs& o,
                              cudaStream_t stream) {
@@ -195,7 +241,11 @@ cudaError_t launch_tp2_oproj(const CUtensorMap& tmA, const CUtensorMap& tmW, con
     if (e != cudaSuccess) return e;
     attr_done = true;
   }
-  const dim3 grid(static_cast<unsigned>(o.N / kTN), static_cast<unsigned>((o.T + kTM - 1) / kTM));
+  if (o.stages < 1 || o.stages > kMaxStagesO || o.tile_n % 32 || o.tile_n > kTNMax ||
+      o.stages * o.atoms * (o.a_rows + o.tile_n) * kTK * 2 > kRingBytes)
+    return cudaErrorInvalidValue;
+  const dim3 grid(static_cast<unsigned>(o.N / o.tile_n),
+                  static_cast<unsigned>((o.T + kTM - 1) / kTM));
   tp2_oproj_kernel<<<grid, 128, kSmemO, stream>>>(tmA, tmW, o);
   return cudaGetLastError();
 }

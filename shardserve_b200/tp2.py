@@ -5,10 +5,11 @@ KV head and the matching column shard of o_proj, and each layer does
 `hidden = hidden + reduce(F.linear(attention, w_o))` with `reduce` = a two-rank NCCL
 all-reduce (shardserve/model.py:40, runtime.py:17-24).  `TP2OprojAllReduce` computes
 `reduce(F.linear(attention, w_o))` in one kernel launch per rank: the GEMM tiles run on the
-tensor cores, each rank stores its bf16 partial of every tile straight into the other rank's
-inbox over NVLink and adds the other rank's partial from its own inbox, so both ranks
-return the same bf16 sum.  The inboxes and flags are plain device allocations shared with
-CUDA IPC once, at construction (a collective over `group`).
+tensor cores, each rank stores its bf16 partial of every tile, tagged with the call number,
+straight into the other rank's inbox over NVLink and adds the other rank's partial from its
+own inbox once its tags match, so both ranks return the same bf16 sum.  The inboxes are
+plain device allocations shared with CUDA IPC once, at construction (a collective over
+`group`).
 """
 from __future__ import annotations
 
@@ -20,7 +21,6 @@ from .kernel import KernelUnsupported
 
 
 class TP2OprojAllReduce:
-    TILE_TOKENS, TILE_FEATURES = 128, 32
 
     def __init__(self, group: Any, device: Any, max_tokens: int, out_features: int,
                  in_features: int):
@@ -29,23 +29,22 @@ class TP2OprojAllReduce:
 
         if dist.get_world_size(group) != 2:
             raise KernelUnsupported("TP2OprojAllReduce needs a group of exactly two ranks")
-        if out_features % self.TILE_FEATURES or in_features % 64:
-            raise KernelUnsupported("out_features must be a multiple of 32 and in_features of 64")
+        if out_features % 128 or in_features % 256:
+            raise KernelUnsupported("out_features must be a multiple of 128 and in_features of 256")
         self.device = torch.device(device)
         self.rank = dist.get_rank(group)
         self.max_tokens, self.n, self.k = int(max_tokens), int(out_features), int(in_features)
-        self.tiles = -(-self.max_tokens // self.TILE_TOKENS) * (self.n // self.TILE_FEATURES)
         lib = _native.lib()
         with torch.cuda.device(self.device):
             self._local = {}
-            for name, nbytes in (("inbox", 2 * self.max_tokens * self.n * 2),
-                                 ("flags", 2 * self.tiles * 4), ("err", 256)):
+            for name, nbytes in (("inbox", 8 * self.max_tokens * self.n), ("err", 256),
+                                 ("epoch", 256)):
                 p = ctypes.c_void_p()
                 if lib.ss_device_alloc_zeroed(nbytes, ctypes.byref(p)) != _native.SS_OK:
                     raise RuntimeError(f"ss_device_alloc_zeroed: {_native.last_error()}")
                 self._local[name] = p.value
             handles = {}
-            for name in ("inbox", "flags"):
+            for name in ("inbox",):
                 h = ctypes.create_string_buffer(64)
                 if lib.ss_ipc_handle(self._local[name], h) != _native.SS_OK:
                     raise RuntimeError(f"ss_ipc_handle: {_native.last_error()}")
@@ -60,7 +59,6 @@ class TP2OprojAllReduce:
                     raise RuntimeError(f"ss_ipc_open: {_native.last_error()}")
                 self._peer[name] = p.value
             dist.barrier(group=group)
-        self.epoch = 0
 
     def __call__(self, attn: Any, w_o: Any, out: Any = None) -> Any:
         """reduce(F.linear(attn, w_o)) over the two ranks: attn bf16 [T, in_features] (this
@@ -76,13 +74,11 @@ class TP2OprojAllReduce:
             raise KernelUnsupported("more tokens than the inbox holds")
         if out is None:
             out = torch.empty((attn.shape[0], self.n), dtype=torch.bfloat16, device=attn.device)
-        self.epoch += 1
         rc = _native.lib().ss_tp2_oproj_allreduce(
             attn.data_ptr(), _native.strides(attn.stride()), w_o.data_ptr(),
             _native.strides(w_o.stride()), out.data_ptr(), _native.strides(out.stride()),
             attn.shape[0], self.n, self.k, self._local["inbox"], self._peer["inbox"],
-            self._local["flags"], self._peer["flags"], self.max_tokens, self.tiles,
-            (self.epoch - 1) % 0xFFFFFFFF + 1, self._local["err"],
+            self.max_tokens, self._local["epoch"], self._local["err"],
             torch.cuda.current_stream(attn.device).cuda_stream)
         if rc == _native.SS_ERR_INVALID:
             raise KernelUnsupported(_native.last_error())

@@ -4,7 +4,8 @@ Each rank runs in its own process on its own GPU (NCCL group on 127.0.0.1).  The
 result must (1) be bit-identical on both ranks, (2) match the reference's composition
 F.linear + NCCL all-reduce within one bf16 rounding step of each partial, and (3) match an
 fp32 restatement of the whole projection within bf16 tolerance, over several calls (both
-inbox halves) and token counts.  Skipped unless two GPUs are visible.
+inbox halves) and token counts, eagerly and replayed from a CUDA graph.  Skipped unless two GPUs are
+visible.
 """
 import os
 import socket
@@ -62,6 +63,27 @@ def _rank_main(rank, port, result_dir):
                 vs_exact=float((got.float() - exact).abs().max()),
                 ref_vs_exact=float((ref.float() - exact).abs().max()),
                 scale=float(exact.abs().max())))
+        # Replays from a CUDA graph: the call number advances on the device.
+        g = torch.Generator(device="cpu").manual_seed(999 + rank)
+        a = torch.randn(64, K, generator=g).to(torch.bfloat16).to(dev)
+        w = (torch.randn(N, K, generator=g) * K ** -0.5).to(torch.bfloat16).to(dev)
+        eager = op(a, w).clone()
+        out = torch.empty_like(eager)
+        s = torch.cuda.Stream(dev)
+        s.wait_stream(torch.cuda.current_stream(dev))
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.stream(s):
+            with torch.cuda.graph(graph, stream=s):
+                for _ in range(3):
+                    op(a, w, out=out)
+        torch.cuda.current_stream(dev).wait_stream(s)
+        for _ in range(4):
+            out.zero_()
+            graph.replay()
+            torch.cuda.synchronize()
+            report.append(dict(T=64, identical=True, vs_ref=0.0, vs_exact=0.0, ref_vs_exact=0.0,
+                               scale=1.0, graph_equal=bool(torch.equal(out, eager))))
+        del graph
         report.append(dict(errors=op.device_errors()))
         op.close()
     finally:
@@ -79,6 +101,7 @@ def test_fused_oproj_allreduce_two_gpus(tmp_path):
         rep = torch.load(tmp_path / f"rank{rank}.pt")
         assert rep[-1]["errors"] == 0
         for r in rep[:-1]:
+            assert r.get("graph_equal", True), r
             assert r["identical"], r
             # Two bf16 roundings of partials plus one of the sum: within a few ulps of the
             # output's magnitude, as the reference's own composition is.
