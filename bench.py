@@ -795,25 +795,36 @@ def run_tp2long(args, rank, world, dist, h):
 
 
 def run_e2e(args, b, dev, h, tokens_all):
-    """Per step: pinned host -> device copies of q, new K/V rows, positions, sequence ids,
-    block tables and slots; Cache.write + ragged_attention_direct through the public API;
-    device -> pinned host copy of the output; stream synchronise (the reference runtime reads
-    its results back every iteration, runtime.py:156)."""
+    """Per step: one pinned host -> device copy of the step's inputs (q, new K/V rows,
+    positions, sequence ids, block tables and slots, packed at 256-byte offsets in one pinned
+    buffer); Cache.write + ragged_attention_direct through the public API on device views of
+    that buffer; device -> pinned host copy of the output; stream synchronise (the reference
+    runtime reads its results back every iteration, runtime.py:156)."""
     import torch
 
     import shardserve_b200 as sb
 
-    host = {k: getattr(b, k).cpu().pin_memory() for k in
-            ("q", "k_new", "v_new", "positions", "seq_ids", "block_tables", "slots")}
-    dev_buf = {k: torch.empty_like(getattr(b, k)) for k in host}
+    names = ("q", "k_new", "v_new", "positions", "seq_ids", "block_tables", "slots")
+    offs, total = {}, 0
+    for k in names:
+        t = getattr(b, k)
+        offs[k] = total
+        total += (t.numel() * t.element_size() + 255) // 256 * 256
+    host_flat = torch.empty(total, dtype=torch.uint8).pin_memory()
+    dev_flat = torch.empty(total, dtype=torch.uint8, device=dev)
+    dev_buf = {}
+    for k in names:
+        t = getattr(b, k)
+        n = t.numel() * t.element_size()
+        host_flat[offs[k]:offs[k] + n].copy_(t.contiguous().view(-1).view(torch.uint8).cpu())
+        dev_buf[k] = dev_flat[offs[k]:offs[k] + n].view(t.dtype).view(t.shape)
     out_host = torch.empty(b.q.shape, dtype=torch.bfloat16).pin_memory()
-    h2d = sum(t.numel() * t.element_size() for t in host.values())
+    h2d = total
     d2h = out_host.numel() * out_host.element_size()
     stream = torch.cuda.current_stream(dev)
 
     def one():
-        for k, t in host.items():
-            dev_buf[k].copy_(t, non_blocking=True)
+        dev_flat.copy_(host_flat, non_blocking=True)
         sb.kv_append(b.k_pool, b.v_pool, dev_buf["k_new"], dev_buf["v_new"], dev_buf["slots"])
         out = sb.ragged_attention_direct(dev_buf["q"], b.k_pool, b.v_pool, dev_buf["block_tables"],
                                          dev_buf["seq_ids"], dev_buf["positions"], SCALE)
@@ -833,7 +844,8 @@ def run_e2e(args, b, dev, h, tokens_all):
     return {"value": tokens_all * args.e2e_steps / (ms / 1e3), "unit": "tok/s",
             "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
             "ms_per_step": ms / args.e2e_steps,
-            "api": "shardserve_b200.kv_append + ragged_attention_direct, eager, per-step sync"}
+            "api": "one packed pinned H2D copy, shardserve_b200.kv_append + "
+                   "ragged_attention_direct (torch binding), D2H of the output, per-step sync"}
 
 
 def traffic_from_profile():

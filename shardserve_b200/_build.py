@@ -75,6 +75,41 @@ def build(force: bool = False, verbose: bool = False, ptxas_info: bool = False) 
     return LIB_PATH
 
 
+# ---- torch-tensor binding of the hot per-layer calls (host C++, torch headers) -------------
+BINDING_NAME = "_shardserve_torch"
+BINDING_SOURCE = os.path.join(CSRC, "torch_binding.cpp")
+BINDING_PATH = os.path.join(PKG_DIR, BINDING_NAME + ".so")
+
+
+def binding_up_to_date() -> bool:
+    if not os.path.exists(BINDING_PATH):
+        return False
+    built = os.path.getmtime(BINDING_PATH)
+    header = os.path.join(REPO_DIR, "include", "shardserve_b200.h")
+    return all(os.path.getmtime(f) <= built for f in (BINDING_SOURCE, header))
+
+
+def build_binding(force: bool = False, verbose: bool = False) -> str:
+    """Compiles csrc/torch_binding.cpp against this interpreter's torch into BINDING_PATH
+    (host code only: no GPU is needed to build it)."""
+    if not force and binding_up_to_date():
+        return BINDING_PATH
+    from torch.utils import cpp_extension
+
+    build_dir = os.path.join(PKG_DIR, "_build", "torch_binding")
+    os.makedirs(build_dir, exist_ok=True)
+    cpp_extension.load(name=BINDING_NAME, sources=[BINDING_SOURCE],
+                       extra_include_paths=[os.path.join(REPO_DIR, "include")],
+                       extra_cflags=["-O2", "-std=c++17"], build_directory=build_dir,
+                       with_cuda=True, verbose=verbose)
+    tmp = BINDING_PATH + ".tmp"
+    shutil.copyfile(os.path.join(build_dir, BINDING_NAME + ".so"), tmp)
+    os.replace(tmp, BINDING_PATH)
+    return BINDING_PATH
+
+
 if __name__ == "__main__":
     build(force="--force" in sys.argv, verbose=True, ptxas_info="--ptxas" in sys.argv)
+    build_binding(force="--force" in sys.argv, verbose=True)
     print(LIB_PATH)
+    print(BINDING_PATH)

@@ -1,8 +1,10 @@
-"""ctypes binding of the in-tree sm_100a library `libshardserve_b200.so`.
+"""Bindings of the in-tree sm_100a library `libshardserve_b200.so`.
 
-The library is the product: every attention / append call goes through it.  There is no
-Python or CPU fallback; if the library is missing this module raises ImportError-like
-errors on first use, naming the build command.
+The library is the product: every attention / append call goes through it.  `lib()` is its
+ctypes binding (the whole C ABI); `ops()` is the torch-tensor binding of the per-layer hot
+calls (`_shardserve_torch.so`, csrc/torch_binding.cpp), which calls the same library through
+the entry-point addresses ctypes resolved.  There is no Python or CPU fallback; if either
+file is missing these raise ImportError-like errors on first use, naming the build command.
 """
 from __future__ import annotations
 
@@ -10,10 +12,11 @@ import ctypes
 import os
 import threading
 
-from ._build import LIB_PATH
+from ._build import BINDING_NAME, BINDING_PATH, LIB_PATH
 
-_lock = threading.Lock()
+_lock = threading.RLock()
 _lib = None
+_ops = None
 
 _i64p = ctypes.POINTER(ctypes.c_int64)
 _vp = ctypes.c_void_p
@@ -105,3 +108,38 @@ def last_error() -> str:
 def strides(seq) -> ctypes.Array:
     arr = (ctypes.c_int64 * len(seq))(*seq)
     return arr
+
+
+_BOUND = ("ss_ragged_paged_attention", "ss_kv_append", "ss_rope_kv_append",
+          "ss_attention_workspace_bytes", "ss_last_error_message")
+
+
+def ops():
+    """Loads (once), binds and returns the torch-tensor binding module."""
+    global _ops
+    if _ops is not None:
+        return _ops
+    with _lock:
+        if _ops is None:
+            import importlib.machinery
+            import importlib.util
+
+            import torch  # noqa: F401  (the binding links against the loaded libtorch)
+
+            from .kernel import KernelUnsupported
+
+            if not os.path.exists(BINDING_PATH):
+                raise NativeLibraryMissing(
+                    f"{BINDING_PATH} is missing; build it with "
+                    "`python -c 'import __graft_entry__ as g; g.build()'` or "
+                    "`python shardserve_b200/_build.py`")
+            loader = importlib.machinery.ExtensionFileLoader(BINDING_NAME, BINDING_PATH)
+            spec = importlib.util.spec_from_file_location(BINDING_NAME, BINDING_PATH,
+                                                          loader=loader)
+            mod = importlib.util.module_from_spec(spec)
+            loader.exec_module(mod)
+            handle = lib()
+            addrs = {n: ctypes.cast(getattr(handle, n), ctypes.c_void_p).value for n in _BOUND}
+            mod.bind(addrs, KernelUnsupported)
+            _ops = mod
+    return _ops

@@ -20,7 +20,7 @@ from typing import Any
 import numpy as np
 
 from . import _native
-from .kernel import KernelUnsupported, _workspaces
+from .kernel import KernelUnsupported, workspace_for
 
 _OUT_KEYS = ("ids", "positions", "tables", "seqs", "slots", "selected")
 
@@ -130,7 +130,7 @@ class DeviceMetadata:
                        selected=torch.empty(len(sel), dtype=torch.long, device=dev))
         else:
             self._check_out(out, n, tokens, len(sel))
-        ws = _workspaces.get(self.device.index)
+        ws = workspace_for(self.device)
         rc = _native.lib().ss_build_metadata(
             self._staged[k].data_ptr(), n, len(sel), tokens, self.store.data_ptr(),
             self.lens.data_ptr(), self.capacity, self.store.stride(0), self.blocks.count,

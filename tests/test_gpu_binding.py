@@ -1,0 +1,104 @@
+"""The torch binding (csrc/torch_binding.cpp) raises the reference wrapper's errors with its
+messages (shardserve/kernel.py:28-49) for inputs that only a CUDA tensor reaches, and the
+calls run through it."""
+import os
+
+import pytest
+import torch
+
+import shardserve_b200 as sb
+from shardserve_b200 import _native
+from shardserve_b200 import kernel as K
+
+pytestmark = pytest.mark.gpu
+
+BF = torch.bfloat16
+
+
+@pytest.fixture(scope="module")
+def dev():
+    assert torch.cuda.is_available(), "GPU tests need a CUDA device"
+    return torch.device("cuda", 0)
+
+
+def _inputs(dev, **over):
+    a = dict(q=torch.zeros(2, 8, 128, dtype=BF, device=dev),
+             k=torch.zeros(4, 16, 1, 128, dtype=BF, device=dev),
+             v=torch.zeros(4, 16, 1, 128, dtype=BF, device=dev),
+             bt=torch.zeros(2, 1, dtype=torch.int32, device=dev),
+             seq=torch.zeros(2, dtype=torch.int32, device=dev),
+             pos=torch.zeros(2, dtype=torch.int64, device=dev))
+    a.update(over)
+    return a
+
+
+def _attn(a):
+    return sb.ragged_attention_direct(a["q"], a["k"], a["v"], a["bt"], a["seq"], a["pos"], 0.1)
+
+
+def test_binding_is_the_in_tree_module():
+    assert os.path.dirname(_native.ops().__file__) == os.path.dirname(_native.LIB_PATH)
+
+
+def _z(*shape, dtype=BF, dev="cuda"):
+    return torch.zeros(*shape, dtype=dtype, device=dev)
+
+
+@pytest.mark.parametrize("make,msg", [
+    (lambda: dict(q=_z(2, 8, 100)), r"ragged q must be \[tokens, heads, 64\|128\], got \(2, 8, 100\)"),
+    (lambda: dict(k=_z(4, 16, 1, 128), v=_z(4, 16, 1, 64)),
+     "ragged K/V pools must have identical rank-4 shapes"),
+    (lambda: dict(k=_z(4, 8, 1, 128), v=_z(4, 8, 1, 128)), "ragged KV pools must be BF16 with block_size=16"),
+    (lambda: dict(k=_z(4, 16, 1, 64), v=_z(4, 16, 1, 64)), "query and KV head dimensions differ"),
+    (lambda: dict(bt=_z(2, dtype=torch.int32)), "block_tables must be a device-resident rank-2 tensor"),
+    (lambda: dict(seq=_z(3, dtype=torch.int32)), "one sequence id and absolute position are required per query"),
+    (lambda: dict(q=_z(0, 8, 128), seq=_z(0, dtype=torch.int32), pos=_z(0, dtype=torch.int64)),
+     "ragged batch cannot be empty"),
+    (lambda: dict(q=_z(2, 3, 128), k=_z(4, 16, 2, 128), v=_z(4, 16, 2, 128)),
+     "query heads must be divisible by KV heads"),
+    (lambda: dict(pos=_z(2, dtype=torch.int64, dev="cpu")), "positions must be on cuda:0"),
+    (lambda: dict(v=_z(4, 16, 1, 128, dtype=torch.float16)), "ragged KV pools must be BF16 with block_size=16"),
+    (lambda: dict(pos=_z(2, dtype=torch.float32)), "positions must be int32 or int64, got torch.float32"),
+    (lambda: dict(bt=_z(2, 1, dtype=torch.int16)), "block_tables must be int32 or int64, got torch.int16"),
+])
+def test_attention_rejections_match_reference(dev, make, msg):
+    with pytest.raises(sb.KernelUnsupported, match=msg):
+        _attn(_inputs(dev, **make()))
+
+
+def test_append_rejections_match_reference(dev):
+    kp = torch.zeros(4, 16, 1, 128, dtype=BF, device=dev)
+    vp = torch.zeros_like(kp)
+    k = torch.zeros(2, 1, 128, dtype=BF, device=dev)
+    slots = torch.zeros(2, dtype=torch.int64, device=dev)
+    with pytest.raises(sb.KernelUnsupported,
+                       match=r"k/v must be \[tokens, 1, 128\], got \(2, 1, 128\)/\(2, 1, 64\)"):
+        sb.kv_append(kp, vp, k, k[:, :, :64], slots)
+    with pytest.raises(sb.KernelUnsupported, match="one slot is required per appended token"):
+        sb.kv_append(kp, vp, k, k, slots[:1])
+    with pytest.raises(sb.KernelUnsupported, match="slots must be on cuda:0"):
+        sb.kv_append(kp, vp, k, k, slots.cpu())
+    with pytest.raises(sb.KernelUnsupported, match="slots must be int32 or int64, got torch.float64"):
+        sb.kv_append(kp, vp, k, k, slots.double())
+
+
+def test_rope_rejections_match_reference(dev):
+    kp = torch.zeros(4, 16, 1, 128, dtype=BF, device=dev)
+    q = torch.zeros(2, 8, 128, dtype=BF, device=dev)
+    k = torch.zeros(2, 1, 128, dtype=BF, device=dev)
+    tab = torch.zeros(8, 128, device=dev)
+    pos = torch.zeros(2, dtype=torch.int64, device=dev)
+    with pytest.raises(sb.KernelUnsupported, match=r"cos must be float32 \[rows, 128\]"):
+        sb.rope_kv_append(q, k, k, tab.double(), tab, pos, kp, kp.clone(), pos)
+    with pytest.raises(sb.KernelUnsupported, match="cos and sin tables must have the same shape"):
+        sb.rope_kv_append(q, k, k, tab, tab[:4], pos, kp, kp.clone(), pos)
+    with pytest.raises(sb.KernelUnsupported, match="out must be a BF16 tensor shaped like q"):
+        sb.rope_kv_append(q, k, k, tab, tab, pos, kp, kp.clone(), pos, out=q[:1])
+
+
+def test_workspace_is_shared_with_the_c_abi_error_reader(dev):
+    inp = _inputs(dev)
+    _attn(inp)
+    ws = K.workspace_for(dev)
+    assert ws is not None and ws.dtype == torch.uint8 and ws.device == dev
+    assert K.device_errors(dev) == 0

@@ -248,6 +248,7 @@ def _big_decode(dev, n_seq, lo, hi, H, KVH, seed):
     (64, 128, 4096, 16, 2),      # batch-64 decode, contexts U[128, 4096]
     (8, 16384, 32768, 8, 1),     # TP2 long-context layout (per rank: 8 q heads, 1 kv head)
     (256, 1, 300, 16, 2),        # many short rows
+    (40000, 1, 16, 16, 2),       # one-page rows: ~90 rows per CTA, more than its row table
 ])
 def test_full_size_decode_against_oracle(dev, n_seq, lo, hi, H, KVH):
     c = _big_decode(dev, n_seq, lo, hi, H, KVH, seed=n_seq + lo)
