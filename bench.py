@@ -822,7 +822,12 @@ def run_e2e(args, b, dev, h, tokens_all):
     positions, sequence ids, block tables and slots, packed at 256-byte offsets in one pinned
     buffer); Cache.write + ragged_attention_direct through the public API on device views of
     that buffer; device -> pinned host copy of the output; stream synchronise (the reference
-    runtime reads its results back every iteration, runtime.py:156)."""
+    runtime reads its results back every iteration, runtime.py:156).
+
+    Measured twice: with append + attention captured once in a CUDA graph over the static
+    input views and replayed each step, as the reference runs its decode steps (static
+    inputs refreshed by copies, then a graph replay: DecodeGraphs, runtime.py:51-80) -- the
+    returned figure -- and with the two calls issued eagerly each step ("eager")."""
     import torch
 
     import shardserve_b200 as sb
@@ -846,29 +851,56 @@ def run_e2e(args, b, dev, h, tokens_all):
     d2h = out_host.numel() * out_host.element_size()
     stream = torch.cuda.current_stream(dev)
 
-    def one():
-        dev_flat.copy_(host_flat, non_blocking=True)
+    def calls():
         sb.kv_append(b.k_pool, b.v_pool, dev_buf["k_new"], dev_buf["v_new"], dev_buf["slots"])
-        out = sb.ragged_attention_direct(dev_buf["q"], b.k_pool, b.v_pool, dev_buf["block_tables"],
-                                         dev_buf["seq_ids"], dev_buf["positions"], SCALE)
+        return sb.ragged_attention_direct(dev_buf["q"], b.k_pool, b.v_pool,
+                                          dev_buf["block_tables"], dev_buf["seq_ids"],
+                                          dev_buf["positions"], SCALE)
+
+    def eager():
+        dev_flat.copy_(host_flat, non_blocking=True)
+        out = calls()
         out_host.copy_(out, non_blocking=True)
         stream.synchronize()
 
-    for _ in range(20):
-        one()
-    h.barrier()
-    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    e0.record(stream)
-    for _ in range(args.e2e_steps):
-        one()
-    e1.record(stream)
-    h.barrier()
-    ms = h.max_over_ranks(e0.elapsed_time(e1))
+    def timed(one):
+        for _ in range(20):
+            one()
+        h.barrier()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        for _ in range(args.e2e_steps):
+            one()
+        e1.record(stream)
+        h.barrier()
+        return h.max_over_ranks(e0.elapsed_time(e1))
+
+    ms_eager = timed(eager)
+    graph = torch.cuda.CUDAGraph()
+    side = torch.cuda.Stream(dev)
+    side.wait_stream(stream)
+    with torch.cuda.stream(side):
+        with torch.cuda.graph(graph, stream=side):
+            out_static = calls()
+    stream.wait_stream(side)
+
+    def replayed():
+        dev_flat.copy_(host_flat, non_blocking=True)
+        graph.replay()
+        out_host.copy_(out_static, non_blocking=True)
+        stream.synchronize()
+
+    ms = timed(replayed)
+    del graph
     return {"value": tokens_all * args.e2e_steps / (ms / 1e3), "unit": "tok/s",
             "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
             "ms_per_step": ms / args.e2e_steps,
-            "api": "one packed pinned H2D copy, shardserve_b200.kv_append + "
-                   "ragged_attention_direct (torch binding), D2H of the output, per-step sync"}
+            "api": "one packed pinned H2D copy into static inputs, replay of a CUDA graph of "
+                   "shardserve_b200.kv_append + ragged_attention_direct, D2H of the output, "
+                   "per-step sync",
+            "eager": {"value": tokens_all * args.e2e_steps / (ms_eager / 1e3), "unit": "tok/s",
+                      "ms_per_step": ms_eager / args.e2e_steps,
+                      "api": "same copies, the two calls issued eagerly (torch binding)"}}
 
 
 def traffic_from_profile():
