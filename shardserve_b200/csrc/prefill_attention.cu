@@ -94,6 +94,7 @@ struct CtlP {
   uint32_t tmem_base;
   int item[2];             // work item of even / odd iterations (from the atomic counter)
   int abort;               // set when a bounded wait timed out: stop after this item
+  int nsub;                // ranked entries present (split ranking)
   int nseg;
   int seg_first[kMaxSeg];  // window-relative first token of each segment
   int seg_last[kMaxSeg];
@@ -161,8 +162,14 @@ __global__ void __launch_bounds__(kThreadsP, 1)
   int* worder = wcost + kMaxWinSort;
   unsigned* sched = a.err + kSchedWord;
   const int nwin = static_cast<int>((a.T + kTQ - 1) / kTQ);
-  const int nitems = nwin * a.KVH;
   const bool ranked = nwin <= kMaxWinSort;
+  // Split ranking: a window whose first and last tokens start different prefill runs is two
+  // entries, its last segment and the rest, so the two halves of a window that straddles
+  // chunks run on different SMs (otherwise it walks the key blocks of both and is the
+  // longest item of the launch).  Entry 2w: the whole window w, or its segments but the last
+  // one; entry 2w + 1: the last segment, or absent (cost -1).
+  const bool split = 2 * nwin <= kMaxWinSort;
+  const int nent = split ? 2 * nwin : nwin;
 
   if (tid == 0) {
     mbar_init(bar(kBarQ), 1);
@@ -180,6 +187,7 @@ __global__ void __launch_bounds__(kThreadsP, 1)
     }
     fence_mbar_init();
     ctl->abort = 0;
+    ctl->nsub = 0;
   }
   if (warp == 0) {
     tmem_alloc(smem_u32(&ctl->tmem_base), kTmemCols);
@@ -201,26 +209,34 @@ __global__ void __launch_bounds__(kThreadsP, 1)
       const long long s0 = seq_at(ts - 1), s1 = seq_at(ts), s2 = seq_at(ts + 1);
       const long long e0 = seq_at(te - 1), e1 = seq_at(te), e2 = seq_at(te + 1);
       const long long ps = ld_index(a.pos, a.pos64, ts), pe = ld_index(a.pos, a.pos64, te);
-      int c = 0;
-      if (e1 == e0 || e1 == e2) c += blocks_of(pe + 1);                  // last segment
-      if (s1 != e1 && (s1 == s0 || s1 == s2)) c += blocks_of(ps + kTQ);  // first segment
-      wcost[w] = c;
+      const int c_last = (e1 == e0 || e1 == e2) ? blocks_of(pe + 1) : 0;  // last segment
+      const int c_first =
+          (s1 != e1 && (s1 == s0 || s1 == s2)) ? blocks_of(ps + kTQ) : 0;   // first segment
+      if (split) {
+        const bool two = c_first > 0 && c_last > 0;
+        wcost[2 * w] = two ? c_first : c_first + c_last;
+        wcost[2 * w + 1] = two ? c_last : -1;
+      } else {
+        wcost[w] = c_first + c_last;
+      }
     }
     __syncthreads();
-    for (int w = tid; w < nwin; w += kThreadsP) {
-      const int c = wcost[w];
+    for (int e = tid; e < nent; e += kThreadsP) {
+      const int c = wcost[e];
       int rank = 0;
-      for (int v = 0; v < nwin; ++v) {
+      for (int v = 0; v < nent; ++v) {
         const int cv = wcost[v];
-        rank += (cv > c) || (cv == c && v < w);
+        rank += (cv > c) || (cv == c && v < e);
       }
-      worder[rank] = w;
+      worder[rank] = e;
+      if (c >= 0) atomicAdd(&ctl->nsub, 1);
     }
   }
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = ctl->tmem_base;
+  const int nitems = (ranked && split ? ctl->nsub : nwin) * a.KVH;
 
   // Per-role running counters: block barriers keep their phases across work items.
   int jg = 0;      // key blocks processed so far by this CTA
@@ -243,7 +259,13 @@ __global__ void __launch_bounds__(kThreadsP, 1)
     ++iter;
     if (item >= nitems || ctl->abort) return ItemInfo{false, 0, 0, 0, 0};
     const int wi = item / a.KVH;
-    const long long t0 = static_cast<long long>(ranked ? worder[wi] : wi) * kTQ;
+    const int ent = ranked ? worder[wi] : wi;
+    int w = ent, part = 0;  // part 0: every segment, 1: all but the last, 2: the last only
+    if (ranked && split) {
+      w = ent >> 1;
+      part = (ent & 1) ? 2 : (wcost[ent | 1] >= 0 ? 1 : 0);
+    }
+    const long long t0 = static_cast<long long>(w) * kTQ;
     const int kvh = item % a.KVH;
     // Segments of this 32-token window: maximal runs of prefill tokens of one sequence.
     if (warp == 2) {
@@ -280,7 +302,19 @@ __global__ void __launch_bounds__(kThreadsP, 1)
         for (int o = 16; o > 0; o >>= 1) v = max(v, __shfl_xor_sync(0xffffffffu, v, o));
         if (lane == 0) ctl->seg_keys[sgi] = v;
       }
-      if (lane == 0) ctl->nseg = nseg;
+      if (lane == 0) {  // keep the segments of this item's part
+        int n = nseg;
+        if (part == 2 && n > 1) {
+          ctl->seg_first[0] = ctl->seg_first[n - 1];
+          ctl->seg_last[0] = ctl->seg_last[n - 1];
+          ctl->seg_seq[0] = ctl->seg_seq[n - 1];
+          ctl->seg_keys[0] = ctl->seg_keys[n - 1];
+          n = 1;
+        } else if (part == 1) {
+          n = n > 0 ? n - 1 : 0;
+        }
+        ctl->nseg = n;
+      }
     }
     named_bar_sync(1, kThreadsP);
     const int nseg = ctl->nseg;
