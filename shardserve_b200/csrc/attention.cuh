@@ -112,15 +112,16 @@ __device__ __forceinline__ bool token_in_long_run(const AttnArgs& a, int min_run
 
 // ---- host-side launchers (defined next to their kernels) ------------------------------
 struct DecodeGeometry {
-  int kvb, ng, nkvblk, G, threads, merge_grid;
+  int kvb, ng, pr, nkvblk, G, threads, merge_grid;
   size_t smem;
   size_t desc_bytes, part_bytes;  // workspace regions
 };
 
 // Geometry of the split-K decode kernel on `device`; false if head_dim/kv layout has no
-// decode kernel instance.
+// decode kernel instance.  `wide`: the launch is followed by prefill tiles, so take the
+// one-CTA-per-SM configuration on half of the SMs when the layout has it.
 bool decode_geometry(int device, long long tokens, int heads, int kv_heads, int head_dim,
-                     DecodeGeometry* g, const char** why);
+                     bool wide, DecodeGeometry* g, const char** why);
 
 // Launches the TMA split-K decode kernel; returns a cudaError_t.
 cudaError_t launch_decode(const DecodeGeometry& g, const CUtensorMap& tmK, const CUtensorMap& tmV,

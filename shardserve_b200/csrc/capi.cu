@@ -422,7 +422,7 @@ int ss_attention_workspace_bytes(int device, int64_t tokens, int heads, int kv_h
   ss::DecodeGeometry g;
   const char* why = "";
   size_t need = ss::kWsHeader;
-  if (ss::decode_geometry(device, tokens, heads, kv_heads, head_dim, &g, &why))
+  if (ss::decode_geometry(device, tokens, heads, kv_heads, head_dim, false, &g, &why))
     need += g.desc_bytes + g.part_bytes;
   *bytes = need;
   return SS_OK;
@@ -487,7 +487,12 @@ int ss_ragged_paged_attention(const void* q, const int64_t q_strides[3], const v
   ss::DecodeGeometry g;
   const char* why = "";
   const bool tma_layout = pool_tma_ok(k_pool, k_pool_strides) && pool_tma_ok(v_pool, v_pool_strides);
-  if (tma_layout && ss::decode_geometry(device, tokens, heads, kv_heads, head_dim, &g, &why)) {
+  // Chunked-prefill tiles when the batch must hold a multi-token run (more query tokens than
+  // sequence rows) and the layout suits the tile kernel; the decode kernel then takes its
+  // wide configuration on half of the SMs so that the tiles start on the other half at once.
+  const bool want_prefill = tokens > bt_rows && ss::prefill_supported(a);
+  if (tma_layout &&
+      ss::decode_geometry(device, tokens, heads, kv_heads, head_dim, want_prefill, &g, &why)) {
     const size_t need = ss::kWsHeader + g.desc_bytes + g.part_bytes;
     if (workspace_bytes < need)
       return fail(SS_ERR_WORKSPACE, "workspace holds %zu bytes, %zu needed", workspace_bytes, need);
@@ -496,11 +501,9 @@ int ss_ragged_paged_attention(const void* q, const int64_t q_strides[3], const v
                         head_dim / 64) &&
         encode_pool_map(&tmV, v_pool, num_pages, kv_heads, head_dim, v_pool_strides, g.kvb,
                         head_dim / 64)) {
-      // Chunked-prefill tiles when the batch must hold a multi-token run (more query tokens
-      // than sequence rows) and the layout suits the tile kernel; otherwise the split-K
-      // kernel computes every token.
+      // Otherwise the split-K kernel computes every token.
       CUtensorMap tmQ, tmKp, tmVp;
-      const bool prefill = tokens > bt_rows && ss::prefill_supported(a) &&
+      const bool prefill = want_prefill &&
                            encode_q_map(&tmQ, q, tokens, heads, head_dim, q_strides) &&
                            encode_pool_map(&tmKp, k_pool, num_pages, kv_heads, head_dim,
                                            k_pool_strides, 1, 1) &&

@@ -17,9 +17,15 @@
 //    base-2 online softmax with quad shuffles, and O^T += V^T.P^T (M = head_dim, N = heads,
 //    K = 16 keys): P goes from the S accumulators straight into the B operand, so the P.V
 //    product wastes no padded rows and the accumulator is head_dim x 8 per warp.
-//  * A token whose pages span several CTAs leaves fp32 partial (m, l, acc) states; after a
-//    CTA has streamed all its pages it takes an atomic ticket per split row, and the last CTA
-//    of a row merges the partials and writes bf16.  No CTA ever waits for another.
+//  * A token whose pages span several CTAs leaves fp32 partial (m, l, acc) states, which the
+//    split-K merge kernel chained after this one (programmatic dependent launch) folds into
+//    bf16 outputs.  No CTA ever waits for another.
+//  * Two CTA shapes.  Decode-only launches: two consumer warps per KV head, 3-4 CTAs per SM
+//    on every SM.  Launches followed by chunked-prefill tiles: the wide CTA (six consumer
+//    warps per KV head, an 8-16 stage ring, one CTA per SM) on only as many SMs as the decode
+//    rows need (~1.3 MB of K/V each, a quarter to three quarters of the SMs); the others
+//    exit after the prologue, so the prefill tiles, which fill a whole SM per CTA, start on
+//    them while the decode rows stream.
 #include <cuda_bf16.h>
 #include <math_constants.h>
 
@@ -34,6 +40,11 @@ namespace ss {
 namespace {
 
 constexpr int kMinChunk = 4;  // pages: lower bound on a CTA's share (limits tiny splits)
+constexpr int kWidePR = 6;    // consumer warps per KV head of the wide configuration
+// Bytes of K/V a wide CTA streams when the decode rows are few: the active wide CTAs are
+// sized so (between a quarter and three quarters of the SMs, the rest exit at once and
+// leave their SMs to the prefill tiles).  ~90 CTAs saturate HBM.
+constexpr long long kWideBytesPerCta = 1344LL << 10;
 
 enum : int { kFirst = 1, kLast = 2, kWhole = 4, kDone = 8, kFirstPartLate = 16 };
 
@@ -58,13 +69,18 @@ struct Ctl {
   long long red[32];
 };
 
-template <int HD, int KVB, int NG>
+// PR = consumer warps per KV head, which take the pages of a segment round robin.  PR = 2
+// (two warps per head, 3-4 CTAs per SM) is the configuration for decode-only launches;
+// PR = 6 is the wide CTA (one per SM, as many bytes in flight and consumer warps as three
+// narrow CTAs) that the chunked-prefill path uses on half of the SMs, so that the prefill
+// tiles run on the other half at the same time.
+template <int HD, int KVB, int NG, int PR>
 struct Traits {
-  static constexpr int kNCW = 2 * KVB;  // consumer warps: (KV head, page parity)
+  static constexpr int kNCW = PR * KVB;  // consumer warps: (KV head, page parity)
   static constexpr int kThreads = 32 * (kNCW + 1);
-  static constexpr int kMinBlocks = KVB == 2 ? 3 : 4;  // CTAs per SM the registers must allow
+  static constexpr int kMinBlocks = PR > 2 ? 1 : (KVB == 2 ? 3 : 4);  // CTAs per SM
   static constexpr int kSlab = kPage * KVB * HD * 2;   // one page of K (or V), KVB heads
-  static constexpr int kStages = KVB == 2 ? 3 : 5;
+  static constexpr int kStages = PR > 2 ? (KVB == 2 ? 8 : 16) : (KVB == 2 ? 3 : 5);
   static constexpr int kStageBytes = 2 * kSlab;
   static constexpr int kRows = 16 * KVB;  // query-head rows per partial slot
   static constexpr int kSlotFloats = kRows * (HD + 2);
@@ -73,7 +89,7 @@ struct Traits {
   static constexpr int kQRows = 8 * NG;  // query-head rows a consumer warp prefetches
   static constexpr int kQBufBytes = kQRows * HD * 2;  // one row block of q, bf16
   static constexpr int kOffMerge = kStages * kStageBytes;
-  static constexpr int kOffQ = kOffMerge + KVB * kMergePerHead * 4;  // [warp][2][kQBufBytes]
+  static constexpr int kOffQ = kOffMerge + KVB * (PR - 1) * kMergePerHead * 4;  // [warp][2][kQBufBytes]
   static constexpr int kOffMeta = kOffQ + kNCW * 2 * kQBufBytes;
   static constexpr int kOffBar = kOffMeta + kStages * (int)sizeof(StageMeta);
   static constexpr int kOffCtl = kOffBar + 2 * kStages * 8;
@@ -184,11 +200,11 @@ __device__ __forceinline__ uint32_t slab_addr(uint32_t slab, int g, int kk, int 
   return slab + row * 128 + ((chunk16 ^ (key & 7)) << 4);
 }
 
-template <int HD, int KVB, int NG>
-__global__ void __launch_bounds__(Traits<HD, KVB, NG>::kThreads, Traits<HD, KVB, NG>::kMinBlocks)
+template <int HD, int KVB, int NG, int PR>
+__global__ void __launch_bounds__(Traits<HD, KVB, NG, PR>::kThreads, Traits<HD, KVB, NG, PR>::kMinBlocks)
     decode_attention_kernel(const __grid_constant__ CUtensorMap tmK,
                             const __grid_constant__ CUtensorMap tmV, const DecodeArgs d) {
-  using Tr = Traits<HD, KVB, NG>;
+  using Tr = Traits<HD, KVB, NG, PR>;
   constexpr int NT = Tr::kThreads;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
@@ -261,7 +277,13 @@ __global__ void __launch_bounds__(Traits<HD, KVB, NG>::kThreads, Traits<HD, KVB,
     long long total;
     long long start = run + block_excl_scan<NT>(s, ctl, total);
     if (a.T <= CH) U = total;  // single pass: the scan also gives the total
-    chunk = max((U + d.G - 1) / d.G, static_cast<long long>(kMinChunk));
+    long long ctas = d.G;  // CTAs that share the units
+    if (PR > 2) {
+      const long long per = max(1LL, kWideBytesPerCta / (2 * Tr::kSlab));
+      const long long lo = max(1, d.G / 4), hi = max(lo, static_cast<long long>(3 * d.G / 4));
+      ctas = min(hi, max(lo, (U + per - 1) / per));
+    }
+    chunk = max((U + ctas - 1) / ctas, static_cast<long long>(kMinChunk));
     u0 = static_cast<long long>(blockIdx.x) * chunk;
     if (u0 >= U) {  // uniform across the CTA; see the wait/trigger order below
       griddep_wait();
@@ -431,8 +453,8 @@ __global__ void __launch_bounds__(Traits<HD, KVB, NG>::kThreads, Traits<HD, KVB,
   // ============================== consumer warps ======================================
   griddep_wait();
   griddep_launch_dependents();
-  const int g = warp >> 1;  // KV head inside the block
-  const int j = warp & 1;   // page parity this warp computes
+  const int g = warp / PR;  // KV head inside the block
+  const int j = warp % PR;  // page parity this warp computes
   const int r = lane >> 2, qd = lane & 3;
   const int group = a.group;
   const float sc = a.scale_log2;
@@ -468,7 +490,7 @@ __global__ void __launch_bounds__(Traits<HD, KVB, NG>::kThreads, Traits<HD, KVB,
 
   int stage = 0;
   uint32_t phase = 0;
-  int pos = 0;  // ring position counter: page `pos` is computed by warp parity pos & 1
+  int pos = 0;  // ring position counter: page `pos` is computed by warp parity pos % PR
   while (true) {
     if (!mbar_wait(bar_full + 8 * stage, phase)) {
       atomicOr(a.err, SS_DEVERR_TIMEOUT);
@@ -525,7 +547,7 @@ __global__ void __launch_bounds__(Traits<HD, KVB, NG>::kThreads, Traits<HD, KVB,
         for (int mt = 0; mt < HD / 16; ++mt)
           acc[n][mt][0] = acc[n][mt][1] = acc[n][mt][2] = acc[n][mt][3] = 0.f;
     }
-    if ((pos & 1) != j) {
+    if ((pos % PR) != j) {
       __syncwarp();
       if (lane == 0) mbar_arrive(bar_empty + 8 * stage);
     } else {
@@ -629,10 +651,11 @@ __global__ void __launch_bounds__(Traits<HD, KVB, NG>::kThreads, Traits<HD, KVB,
       l1 += __shfl_xor_sync(0xffffffffu, l1, 1);
       l1 += __shfl_xor_sync(0xffffffffu, l1, 2);
     }
-    float* mg = merge + g * Tr::kMergePerHead;
-    float* mg_m = mg + 32 * Tr::kAccPerThread;
-    float* mg_l = mg_m + 16;
-    if (j == 1) {  // publish the odd-page state of this head
+    float* mgh = merge + g * (PR - 1) * Tr::kMergePerHead;  // this head's PR - 1 slots
+    if (j != 0) {  // publish this warp's page-parity state into slot j - 1
+      float* mg = mgh + (j - 1) * Tr::kMergePerHead;
+      float* mg_m = mg + 32 * Tr::kAccPerThread;
+      float* mg_l = mg_m + 16;
 #pragma unroll
       for (int n = 0; n < NG; ++n)
 #pragma unroll
@@ -651,43 +674,57 @@ __global__ void __launch_bounds__(Traits<HD, KVB, NG>::kThreads, Traits<HD, KVB,
     named_bar_sync(1, Tr::kNCW * 32);
     const bool whole = (m.flags & kWhole) != 0;
     if (j == 0) {
-      // Merge the two page-parity states of head row r (and r + 8).
-      const float mo = mg_m[r];
-      const float M = fmaxf(m0, mo);
-      const float Ms = M == -CUDART_INF_F ? 0.f : M;
-      const float e = ex2(m0 - Ms), eo = ex2(mo - Ms);
-      const float L = l0 * e + mg_l[r] * eo;
-      float M8 = 0.f, e8 = 1.f, eo8 = 0.f, L8 = 0.f;
-      if (NG == 2) {
-        const float mo8 = mg_m[r + 8];
-        M8 = fmaxf(m1, mo8);
-        const float Ms8 = M8 == -CUDART_INF_F ? 0.f : M8;
-        e8 = ex2(m1 - Ms8);
-        eo8 = ex2(mo8 - Ms8);
-        L8 = l1 * e8 + mg_l[r + 8] * eo8;
+      // Fold the other page-parity states of head row r (and r + 8) into this warp's.
+      float M = m0, L = l0, M8 = m1, L8 = l1;
+#pragma unroll
+      for (int sl = 0; sl < PR - 1; ++sl) {
+        const float* mg = mgh + sl * Tr::kMergePerHead;
+        const float* mg_m = mg + 32 * Tr::kAccPerThread;
+        const float* mg_l = mg_m + 16;
+        const float mo = mg_m[r];
+        const float Mn = fmaxf(M, mo);
+        const float Ms = Mn == -CUDART_INF_F ? 0.f : Mn;
+        const float e = ex2(M - Ms), eo = ex2(mo - Ms);
+        L = L * e + mg_l[r] * eo;
+        M = Mn;
+        float e8 = 1.f, eo8 = 0.f;
+        if (NG == 2) {
+          const float mo8 = mg_m[r + 8];
+          const float Mn8 = fmaxf(M8, mo8);
+          const float Ms8 = Mn8 == -CUDART_INF_F ? 0.f : Mn8;
+          e8 = ex2(M8 - Ms8);
+          eo8 = ex2(mo8 - Ms8);
+          L8 = L8 * e8 + mg_l[r + 8] * eo8;
+          M8 = Mn8;
+        }
+        // Per-column (query head) factors of the O^T fragments: heads 2qd and 2qd + 1.
+        float E[NG][2], EO[NG][2];
+#pragma unroll
+        for (int c = 0; c < 2; ++c) {
+          const int src = (2 * qd + c) * 4;
+          E[0][c] = __shfl_sync(0xffffffffu, e, src);
+          EO[0][c] = __shfl_sync(0xffffffffu, eo, src);
+          if (NG == 2) {
+            E[NG - 1][c] = __shfl_sync(0xffffffffu, e8, src);
+            EO[NG - 1][c] = __shfl_sync(0xffffffffu, eo8, src);
+          }
+        }
+#pragma unroll
+        for (int n = 0; n < NG; ++n)
+#pragma unroll
+          for (int mt = 0; mt < HD / 16; ++mt)
+#pragma unroll
+            for (int i = 0; i < 4; ++i)
+              acc[n][mt][i] = acc[n][mt][i] * E[n][i & 1] +
+                              mg[((n * (HD / 16) + mt) * 4 + i) * 32 + lane] * EO[n][i & 1];
       }
-      // Per-column (query head) factors of the O^T fragments: heads 2qd and 2qd + 1.
-      float E[NG][2], EO[NG][2], LL[NG][2];
+      float LL[NG][2];
 #pragma unroll
       for (int c = 0; c < 2; ++c) {
         const int src = (2 * qd + c) * 4;
-        E[0][c] = __shfl_sync(0xffffffffu, e, src);
-        EO[0][c] = __shfl_sync(0xffffffffu, eo, src);
         LL[0][c] = __shfl_sync(0xffffffffu, L, src);
-        if (NG == 2) {
-          E[NG - 1][c] = __shfl_sync(0xffffffffu, e8, src);
-          EO[NG - 1][c] = __shfl_sync(0xffffffffu, eo8, src);
-          LL[NG - 1][c] = __shfl_sync(0xffffffffu, L8, src);
-        }
+        if (NG == 2) LL[NG - 1][c] = __shfl_sync(0xffffffffu, L8, src);
       }
-#pragma unroll
-      for (int n = 0; n < NG; ++n)
-#pragma unroll
-        for (int mt = 0; mt < HD / 16; ++mt)
-#pragma unroll
-          for (int i = 0; i < 4; ++i)
-            acc[n][mt][i] = acc[n][mt][i] * E[n][i & 1] +
-                            mg[((n * (HD / 16) + mt) * 4 + i) * 32 + lane] * EO[n][i & 1];
       if (whole) {
         __nv_bfloat16* ot = a.out + static_cast<long long>(m.t) * a.o_st;
 #pragma unroll
@@ -879,9 +916,9 @@ struct CachedOcc {
   int blocks = 0;
 };
 
-template <int HD, int KVB, int NG>
+template <int HD, int KVB, int NG, int PR>
 int occupancy(int device, const char** why) {
-  using Tr = Traits<HD, KVB, NG>;
+  using Tr = Traits<HD, KVB, NG, PR>;
   static std::mutex mu;
   static CachedOcc cache[16];
   std::lock_guard<std::mutex> lock(mu);
@@ -893,7 +930,7 @@ int occupancy(int device, const char** why) {
   int prev = 0;
   cudaGetDevice(&prev);
   if (prev != device) cudaSetDevice(device);
-  auto fn = decode_attention_kernel<HD, KVB, NG>;
+  auto fn = decode_attention_kernel<HD, KVB, NG, PR>;
   cudaError_t e = cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, Tr::kSmemBytes);
   if (e == cudaSuccess)
     e = cudaFuncSetAttribute(fn, cudaFuncAttributePreferredSharedMemoryCarveout,
@@ -917,31 +954,33 @@ int sm_count(int device) {
   return sms;
 }
 
-template <int HD, int KVB, int NG>
+template <int HD, int KVB, int NG, int PR>
 size_t partial_bytes_of(int device, const char** why) {
-  return static_cast<size_t>(2) * sm_count(device) * occupancy<HD, KVB, NG>(device, why) *
-         Traits<HD, KVB, NG>::kSlotFloats * sizeof(float);
+  return static_cast<size_t>(2) * sm_count(device) * occupancy<HD, KVB, NG, PR>(device, why) *
+         Traits<HD, KVB, NG, PR>::kSlotFloats * sizeof(float);
 }
 
 // The partial-state region is sized for the largest kernel instance, so its size and the
 // offset of the descriptor region behind it are the same for every call on a device.
 size_t partial_region_bytes(int device, const char** why) {
   size_t m = 0;
-  m = std::max(m, partial_bytes_of<128, 2, 1>(device, why));
-  m = std::max(m, partial_bytes_of<128, 2, 2>(device, why));
-  m = std::max(m, partial_bytes_of<128, 1, 1>(device, why));
-  m = std::max(m, partial_bytes_of<128, 1, 2>(device, why));
-  m = std::max(m, partial_bytes_of<64, 2, 1>(device, why));
-  m = std::max(m, partial_bytes_of<64, 2, 2>(device, why));
-  m = std::max(m, partial_bytes_of<64, 1, 1>(device, why));
-  m = std::max(m, partial_bytes_of<64, 1, 2>(device, why));
+  m = std::max(m, partial_bytes_of<128, 2, 1, 2>(device, why));
+  m = std::max(m, partial_bytes_of<128, 2, 2, 2>(device, why));
+  m = std::max(m, partial_bytes_of<128, 1, 1, 2>(device, why));
+  m = std::max(m, partial_bytes_of<128, 1, 2, 2>(device, why));
+  m = std::max(m, partial_bytes_of<64, 2, 1, 2>(device, why));
+  m = std::max(m, partial_bytes_of<64, 2, 2, 2>(device, why));
+  m = std::max(m, partial_bytes_of<64, 1, 1, 2>(device, why));
+  m = std::max(m, partial_bytes_of<64, 1, 2, 2>(device, why));
+  m = std::max(m, partial_bytes_of<128, 2, 1, kWidePR>(device, why));
+  m = std::max(m, partial_bytes_of<128, 1, 1, kWidePR>(device, why));
   return align_up(m, 256);
 }
 
-template <int HD, int KVB, int NG>
+template <int HD, int KVB, int NG, int PR>
 bool geometry_for(int device, long long tokens, int kv_heads, DecodeGeometry* g, const char** why) {
-  using Tr = Traits<HD, KVB, NG>;
-  const int per_sm = occupancy<HD, KVB, NG>(device, why);
+  using Tr = Traits<HD, KVB, NG, PR>;
+  const int per_sm = occupancy<HD, KVB, NG, PR>(device, why);
   if (per_sm <= 0) return false;
   const int sms = sm_count(device);
   if (sms <= 0) {
@@ -950,7 +989,11 @@ bool geometry_for(int device, long long tokens, int kv_heads, DecodeGeometry* g,
   }
   g->kvb = KVB;
   g->ng = NG;
+  g->pr = PR;
   g->nkvblk = kv_heads / KVB;
+  // The wide configuration has one CTA per SM; the kernel keeps as many of them as its
+  // decode rows need (between a quarter and three quarters) and leaves the other SMs to the
+  // prefill tiles launched after it.
   g->G = sms * per_sm;
   g->threads = Tr::kThreads;
   g->smem = Tr::kSmemBytes;
@@ -961,16 +1004,18 @@ bool geometry_for(int device, long long tokens, int kv_heads, DecodeGeometry* g,
 }
 
 template <int HD, int KVB>
-bool geometry_ng(int device, long long tokens, int kv_heads, int group, DecodeGeometry* g,
-                 const char** why) {
-  return group <= 8 ? geometry_for<HD, KVB, 1>(device, tokens, kv_heads, g, why)
-                    : geometry_for<HD, KVB, 2>(device, tokens, kv_heads, g, why);
+bool geometry_ng(int device, long long tokens, int kv_heads, int group, bool wide,
+                 DecodeGeometry* g, const char** why) {
+  if (wide && HD == 128 && group <= 8)
+    return geometry_for<128, KVB, 1, kWidePR>(device, tokens, kv_heads, g, why);
+  return group <= 8 ? geometry_for<HD, KVB, 1, 2>(device, tokens, kv_heads, g, why)
+                    : geometry_for<HD, KVB, 2, 2>(device, tokens, kv_heads, g, why);
 }
 
 }  // namespace
 
 bool decode_geometry(int device, long long tokens, int heads, int kv_heads, int head_dim,
-                     DecodeGeometry* g, const char** why) {
+                     bool wide, DecodeGeometry* g, const char** why) {
   const int group = heads / kv_heads;
   if (group > 16) {
     *why = "more than 16 query heads per KV head";
@@ -978,12 +1023,12 @@ bool decode_geometry(int device, long long tokens, int heads, int kv_heads, int 
   }
   const bool pair = (kv_heads % 2) == 0;
   if (head_dim == 128) {
-    return pair ? geometry_ng<128, 2>(device, tokens, kv_heads, group, g, why)
-                : geometry_ng<128, 1>(device, tokens, kv_heads, group, g, why);
+    return pair ? geometry_ng<128, 2>(device, tokens, kv_heads, group, wide, g, why)
+                : geometry_ng<128, 1>(device, tokens, kv_heads, group, wide, g, why);
   }
   if (head_dim == 64) {
-    return pair ? geometry_ng<64, 2>(device, tokens, kv_heads, group, g, why)
-                : geometry_ng<64, 1>(device, tokens, kv_heads, group, g, why);
+    return pair ? geometry_ng<64, 2>(device, tokens, kv_heads, group, wide, g, why)
+                : geometry_ng<64, 1>(device, tokens, kv_heads, group, wide, g, why);
   }
   *why = "head_dim must be 64 or 128";
   return false;
@@ -1002,17 +1047,19 @@ cudaError_t launch_decode(const DecodeGeometry& g, const CUtensorMap& tmK, const
   cfg.attrs = attr;
   cfg.numAttrs = 1;
   const int hd = d.a.D;
-#define SS_LAUNCH(HD_, KVB_, NG_)                                                              \
-  if (hd == HD_ && g.kvb == KVB_ && g.ng == NG_)                                              \
-    return cudaLaunchKernelEx(&cfg, decode_attention_kernel<HD_, KVB_, NG_>, tmK, tmV, d);
-  SS_LAUNCH(128, 2, 1)
-  SS_LAUNCH(128, 2, 2)
-  SS_LAUNCH(128, 1, 1)
-  SS_LAUNCH(128, 1, 2)
-  SS_LAUNCH(64, 2, 1)
-  SS_LAUNCH(64, 2, 2)
-  SS_LAUNCH(64, 1, 1)
-  SS_LAUNCH(64, 1, 2)
+#define SS_LAUNCH(HD_, KVB_, NG_, PR_)                                                         \
+  if (hd == HD_ && g.kvb == KVB_ && g.ng == NG_ && g.pr == PR_)                               \
+    return cudaLaunchKernelEx(&cfg, decode_attention_kernel<HD_, KVB_, NG_, PR_>, tmK, tmV, d);
+  SS_LAUNCH(128, 2, 1, 2)
+  SS_LAUNCH(128, 2, 2, 2)
+  SS_LAUNCH(128, 1, 1, 2)
+  SS_LAUNCH(128, 1, 2, 2)
+  SS_LAUNCH(64, 2, 1, 2)
+  SS_LAUNCH(64, 2, 2, 2)
+  SS_LAUNCH(64, 1, 1, 2)
+  SS_LAUNCH(64, 1, 2, 2)
+  SS_LAUNCH(128, 2, 1, kWidePR)
+  SS_LAUNCH(128, 1, 1, kWidePR)
 #undef SS_LAUNCH
   return cudaErrorInvalidValue;
 }
