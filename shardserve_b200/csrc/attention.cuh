@@ -46,6 +46,7 @@ struct DecodeArgs {
   int nkvblk;    // KVH / kvb
   int G;         // CTAs in the grid
   int min_run;   // see token_in_long_run(); 0 = this launch owns every token
+  int lo_ctas;   // wide shape: fewest CTAs that share the decode units (a quarter of the SMs)
   int4* desc;    // [T * nkvblk] split descriptor per row: {parts (0 none, 1 whole), first
                  // CTA, first part in the CTA's second slot, 0}; rewritten every call
   float* part;   // [2 * G] partial-state slots
@@ -67,10 +68,9 @@ struct TokInfo {
 //  * seq outside [0, B)          -> no keys (output zeros), SS_DEVERR_SEQ
 //  * position < 0                -> no keys (output zeros), SS_DEVERR_POS
 //  * position + 1 > 16 * W       -> keys clamped to the 16 * W the table can name, SS_DEVERR_POS
-__device__ __forceinline__ TokInfo token_info(const AttnArgs& a, long long t, bool report) {
+__device__ __forceinline__ TokInfo token_info_from(const AttnArgs& a, long long seq, long long pos,
+                                                   bool report) {
   TokInfo r;
-  const long long seq = ld_index(a.seq, a.seq64, t);
-  const long long pos = ld_index(a.pos, a.pos64, t);
   unsigned e = 0;
   long long L = pos + 1;
   if (seq < 0 || seq >= a.B) {
@@ -89,6 +89,9 @@ __device__ __forceinline__ TokInfo token_info(const AttnArgs& a, long long t, bo
   r.L = static_cast<int>(L);
   r.npages = static_cast<int>((L + kPage - 1) / kPage);
   return r;
+}
+__device__ __forceinline__ TokInfo token_info(const AttnArgs& a, long long t, bool report) {
+  return token_info_from(a, ld_index(a.seq, a.seq64, t), ld_index(a.pos, a.pos64, t), report);
 }
 
 // Chunked-prefill tokens: a token belongs to a "long run" when at least `min_run`
@@ -122,6 +125,10 @@ struct DecodeGeometry {
 // one-CTA-per-SM configuration on half of the SMs when the layout has it.
 bool decode_geometry(int device, long long tokens, int heads, int kv_heads, int head_dim,
                      bool wide, DecodeGeometry* g, const char** why);
+// Wide shape: the grid for a launch whose block table has `rows` x `cols` entries (an upper
+// bound of its decode pages), between a quarter and three quarters of the SMs; sets g->G and
+// returns the lower bound the kernel keeps (DecodeArgs::lo_ctas).
+int wide_grid(DecodeGeometry* g, int device, long long rows, long long cols);
 
 // Launches the TMA split-K decode kernel; returns a cudaError_t.
 cudaError_t launch_decode(const DecodeGeometry& g, const CUtensorMap& tmK, const CUtensorMap& tmV,

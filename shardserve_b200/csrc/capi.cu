@@ -513,8 +513,10 @@ int ss_ragged_paged_attention(const void* q, const int64_t q_strides[3], const v
       d.a = a;
       d.kvb = g.kvb;
       d.nkvblk = g.nkvblk;
-      d.G = g.G;
       d.min_run = prefill ? ss::prefill_min_run() : 0;
+      d.lo_ctas = g.G;
+      if (g.pr > 2) d.lo_ctas = ss::wide_grid(&g, device, bt_rows, bt_cols);
+      d.G = g.G;
       uint8_t* ws = static_cast<uint8_t*>(workspace);
       d.part = reinterpret_cast<float*>(ws + ss::kWsHeader);
       d.desc = reinterpret_cast<int4*>(ws + ss::kWsHeader + g.part_bytes);

@@ -66,6 +66,7 @@ struct Ctl {
   long long r0;  // first row (token * nkvblk + block)
   int off0;      // first page inside r0
   int found;
+  unsigned long long stage_bar;  // mbarrier of the staged index arrays (wide shape)
   long long red[32];
 };
 
@@ -230,6 +231,13 @@ __global__ void __launch_bounds__(Traits<HD, KVB, NG, PR>::kThreads, Traits<HD, 
     prefetch_tensormap(&tmK);
     prefetch_tensormap(&tmV);
   }
+  if constexpr (PR > 2) {
+    // Wide shape: the prefill tiles launched after this grid need none of its results, only
+    // the pool pages the preceding append writes.  Wait for the append here and let them
+    // start at once (on the SMs this grid leaves free) instead of after the prologue.
+    griddep_wait();
+    griddep_launch_dependents();
+  }
 
   // ---- prologue: total units, this CTA's range, and its first (row, page) ------------
   // Tokens without units in this launch get their split descriptor cleared (and, for
@@ -237,14 +245,106 @@ __global__ void __launch_bounds__(Traits<HD, KVB, NG, PR>::kThreads, Traits<HD, 
   constexpr int ITEMS = 4;
   constexpr int CH = NT * ITEMS;
   auto note_empty = [&](long long t, long long u) {
-    if (t % d.G != blockIdx.x) return;
+    // t < 2^31 (token indices are int in the stage metadata): a 32-bit modulo
+    if (static_cast<unsigned>(t) % static_cast<unsigned>(d.G) != blockIdx.x) return;
     for (int b = 0; b < d.nkvblk; ++b) d.desc[t * d.nkvblk + b] = make_int4(0, 0, 0, 0);
     if (u < 0) write_zero_token(a, t);
   };
+  long long U = 0, chunk = 0, u0 = 0;
+  // Wide shape: the launch carries thousands of prefill tokens, and a scan that loads them
+  // token by token (several dependent round trips per pass, several passes) kept the
+  // tiles waiting ~13 us.  Instead the sequence-id and position arrays are copied whole into
+  // the idle stage ring (one bulk copy each) and scanned from shared memory by rolled loops.
+  bool staged = false;
+  if constexpr (PR > 2) {
+    const long long bs = a.T * (a.seq64 ? 8 : 4), bp = a.T * (a.pos64 ? 8 : 4);
+    const long long offp = (bs + 15) & ~15LL;
+    staged = offp + bp <= static_cast<long long>(Tr::kStages) * Tr::kStageBytes &&
+             (reinterpret_cast<uintptr_t>(a.seq) & 15) == 0 &&
+             (reinterpret_cast<uintptr_t>(a.pos) & 15) == 0;
+    if (staged) {
+      uint8_t* ss = smem;
+      uint8_t* sp = smem + offp;
+      const uint32_t sbar = smem_u32(&ctl->stage_bar);
+      const long long bs16 = bs & ~15LL, bp16 = bp & ~15LL;
+      if (tid == 0) {
+        mbar_init(sbar, 1);
+        fence_mbar_init();
+        mbar_arrive_expect_tx(sbar, static_cast<uint32_t>(bs16 + bp16));
+        if (bs16) bulk_load(smem_u32(ss), a.seq, static_cast<uint32_t>(bs16), sbar);
+        if (bp16) bulk_load(smem_u32(sp), a.pos, static_cast<uint32_t>(bp16), sbar);
+      }
+      const uint8_t* gs = static_cast<const uint8_t*>(a.seq);
+      const uint8_t* gp = static_cast<const uint8_t*>(a.pos);
+      for (long long i = bs16 + tid; i < bs; i += NT) ss[i] = gs[i];  // tails (< 16 bytes)
+      for (long long i = bp16 + tid; i < bp; i += NT) sp[i] = gp[i];
+      __syncthreads();  // barrier initialised, tails stored
+      if (__syncthreads_or(!mbar_wait(sbar, 0))) {  // CTA-uniform
+        if (tid == 0) atomicOr(a.err, SS_DEVERR_TIMEOUT);
+        mbar_wait(sbar, 0);  // let the copies land before the CTA releases its memory
+        griddep_wait();
+        return;
+      }
+      auto seq_at = [&](long long t) -> long long {
+        return a.seq64 ? reinterpret_cast<const long long*>(ss)[t]
+                       : static_cast<long long>(reinterpret_cast<const int*>(ss)[t]);
+      };
+      auto pos_at = [&](long long t) -> long long {
+        return a.pos64 ? reinterpret_cast<const long long*>(sp)[t]
+                       : static_cast<long long>(reinterpret_cast<const int*>(sp)[t]);
+      };
+      // token_units from the staged arrays (same predicate as token_in_long_run).
+      auto units = [&](long long t, bool report, int* np_out) -> long long {
+        const long long sq = seq_at(t);
+        const TokInfo ti = token_info_from(a, sq, pos_at(t), report);
+        bool in_run = false;
+        if (d.min_run > 0) {
+          int n = 1;
+          for (long long j = t - 1; j >= 0 && n < d.min_run && seq_at(j) == sq; --j) ++n;
+          for (long long j = t + 1; j < a.T && n < d.min_run && seq_at(j) == sq; ++j) ++n;
+          in_run = n >= d.min_run;
+        }
+        const int np = in_run ? 0 : ti.npages;
+        if (np_out) *np_out = np;
+        if (!in_run && np == 0) return -1;
+        return static_cast<long long>(np) * d.nkvblk;
+      };
+      const long long per = (a.T + NT - 1) / NT;  // consecutive tokens per thread
+      const long long tb = static_cast<long long>(tid) * per, te = min(a.T, tb + per);
+      long long s = 0;
+#pragma unroll 1
+      for (long long t = tb; t < te; ++t) {
+        const long long u = units(t, blockIdx.x == 0, nullptr);
+        if (u <= 0) note_empty(t, u);
+        s += u > 0 ? u : 0;
+      }
+      long long start = block_excl_scan<NT>(s, ctl, U);
+      const long long per_cta = max(1LL, kWideBytesPerCta / (2 * Tr::kSlab));
+      const long long ctas = min(static_cast<long long>(d.G),
+                                 max(static_cast<long long>(d.lo_ctas), (U + per_cta - 1) / per_cta));
+      chunk = max((U + ctas - 1) / ctas, static_cast<long long>(kMinChunk));
+      u0 = static_cast<long long>(blockIdx.x) * chunk;
+      if (u0 >= U) {  // uniform across the CTA; see the wait/trigger order below
+        griddep_wait();
+        return;
+      }
+#pragma unroll 1
+      for (long long t = tb; t < te; ++t) {
+        int np = 0;
+        const long long u = units(t, false, &np);
+        if (u > 0 && start <= u0 && u0 < start + u) {
+          const long long off = u0 - start;
+          ctl->r0 = t * d.nkvblk + off / np;
+          ctl->off0 = static_cast<int>(off % np);
+          ctl->found = 1;
+        }
+        start += u > 0 ? u : 0;
+      }
+    }
+  }
   long long us[ITEMS];
   int nps[ITEMS];
-  long long U = 0;
-  if (a.T > CH) {  // large batches: a first pass for the total only
+  if (!staged && a.T > CH) {  // large batches: a first pass for the total only
     for (long long base = 0; base < a.T; base += CH) {
       long long s = 0;
 #pragma unroll
@@ -259,8 +359,8 @@ __global__ void __launch_bounds__(Traits<HD, KVB, NG, PR>::kThreads, Traits<HD, 
       U += block_sum<NT>(s, ctl);
     }
   }
-  long long run = 0, chunk = 0, u0 = 0;
-  for (long long base = 0; base < a.T; base += CH) {
+  long long run = 0;
+  for (long long base = 0; base < a.T && !staged; base += CH) {
     long long s = 0;
 #pragma unroll
     for (int i = 0; i < ITEMS; ++i) {
@@ -280,8 +380,7 @@ __global__ void __launch_bounds__(Traits<HD, KVB, NG, PR>::kThreads, Traits<HD, 
     long long ctas = d.G;  // CTAs that share the units
     if (PR > 2) {
       const long long per = max(1LL, kWideBytesPerCta / (2 * Tr::kSlab));
-      const long long lo = max(1, d.G / 4), hi = max(lo, static_cast<long long>(3 * d.G / 4));
-      ctas = min(hi, max(lo, (U + per - 1) / per));
+      ctas = min(static_cast<long long>(d.G), max(static_cast<long long>(d.lo_ctas), (U + per - 1) / per));
     }
     chunk = max((U + ctas - 1) / ctas, static_cast<long long>(kMinChunk));
     u0 = static_cast<long long>(blockIdx.x) * chunk;
@@ -1013,6 +1112,16 @@ bool geometry_ng(int device, long long tokens, int kv_heads, int group, bool wid
 }
 
 }  // namespace
+
+int wide_grid(DecodeGeometry* g, int device, long long rows, long long cols) {
+  const int sms = sm_count(device);
+  const int lo = std::max(1, sms / 4), hi = std::max(lo, 3 * sms / 4);
+  const long long slab = static_cast<long long>(kPage) * g->kvb * 128 * 2;
+  const long long per = std::max(1LL, kWideBytesPerCta / (2 * slab));
+  const long long bound = rows * cols * g->nkvblk;  // decode pages at most
+  g->G = static_cast<int>(std::min<long long>(hi, std::max<long long>(lo, (bound + per - 1) / per)));
+  return lo;
+}
 
 bool decode_geometry(int device, long long tokens, int heads, int kv_heads, int head_dim,
                      bool wide, DecodeGeometry* g, const char** why) {

@@ -368,3 +368,31 @@ def test_prefill_work_queue_spans_more_items_than_sms(dev):
     again, _, _ = _ragged_rows_case(dev, rows, 16, 2, seed=34)
     assert torch.equal(again, out)
     assert K.device_errors(dev) == 0
+
+
+@pytest.mark.parametrize("seq_dtype,pos_dtype", [(torch.int32, torch.int64), (torch.int64, torch.int32)])
+def test_mixed_batch_index_arrays_staged_or_not_give_identical_results(dev, seq_dtype, pos_dtype):
+    """The wide decode shape next to the prefill tiles copies 16-byte aligned sequence-id and
+    position arrays into shared memory for its scan, and scans them from global memory
+    otherwise.  The same batch with the arrays as offset views (not 16-byte aligned) must give
+    bit-identical outputs."""
+    from shardserve_b200.workloads import ragged_batch
+
+    g = torch.Generator().manual_seed(41)
+    decode = [(int(c) - 1, 1) for c in torch.randint(256, 4097, (24,), generator=g)]
+    prefill = [(int(c), 512) for c in torch.randint(0, 2049, (3,), generator=g)]
+    b = ragged_batch(decode + prefill, 16, 2, 128, seed=41, device=dev)
+    seq = b.seq_ids.to(seq_dtype)
+    pos = b.positions.to(pos_dtype)
+    args = (b.q, b.k_pool, b.v_pool, b.block_tables)
+    aligned = sb.ragged_attention_direct(*args, seq, pos, 128 ** -0.5)
+    assert K.last_attention_path() == 3
+    T = seq.numel()
+    seq_off = torch.empty(T + 1, dtype=seq_dtype, device=dev)[1:]
+    pos_off = torch.empty(T + 1, dtype=pos_dtype, device=dev)[1:]
+    seq_off.copy_(seq)
+    pos_off.copy_(pos)
+    assert seq_off.data_ptr() % 16 and pos_off.data_ptr() % 16
+    offset = sb.ragged_attention_direct(*args, seq_off, pos_off, 128 ** -0.5)
+    assert torch.equal(aligned, offset)
+    assert K.device_errors(dev) == 0
