@@ -69,7 +69,10 @@ constexpr int kRegsProducer = 72, kRegsSoftmax = 216;
 static_assert(128 * kRegsProducer + 256 * kRegsSoftmax <= kThreadsP * kLaunchRegs,
               "setmaxnreg split exceeds the launch register pool");
 constexpr int kMinRunP = 2;                    // tokens of runs >= 2 are prefill tokens
-constexpr int kPolyEvery = 4;                  // one exponential pair in 4 on the FMA pipe
+// One exponential pair in 3 on the FMA pipe.  The row sum accumulates pair i into acc[i % 4],
+// so with 3 the slow polynomial results spread over all four partial sums; with 4 they all
+// fell into one and formed a serial chain (the prefill-only step was 72.4 us against 67.9).
+constexpr int kPolyEvery = 3;
 constexpr uint32_t kTmemCols = 512;            // S_0 S_1 [0,256), O_0 O_1 [256,512)
 constexpr uint32_t kColO = 256;
 
