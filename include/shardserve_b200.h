@@ -150,12 +150,11 @@ SS_API int ss_build_metadata(const int64_t* packed, int64_t rows, int64_t n_sele
  *               (ss_device_alloc_zeroed) and never cleared again
  * epoch_counter: 8 zeroed device bytes per rank that count its calls (the kernel advances
  *               them, so calls can be replayed from a CUDA graph)
- * out_features a multiple of 128, in_features of 256.  Tiles are 128 tokens x 32-128
- * features (wider for more tokens); all tiles of a call must fit one wave of the GPU
- * (tiles <= SM count).  workspace: the
- * 4-byte error word (a partner that does not arrive within ~1 s sets SS_DEVERR_TIMEOUT
- * instead of hanging).  Calls on one rank are stream-ordered; the two ranks' n-th calls
- * run concurrently.
+ * out_features a multiple of 128, in_features of 256.  Tiles are 128 tokens x 32
+ * features; all tiles of a call must fit one wave of the GPU (tiles <= SM count, so
+ * ceil(tokens / 128) * out_features / 32 <= SMs).  workspace: the 4-byte error word (a
+ * partner that does not arrive within ~1 s sets SS_DEVERR_TIMEOUT instead of hanging).
+ * Calls on one rank are stream-ordered; the two ranks' n-th calls run concurrently.
  */
 SS_API int ss_tp2_oproj_allreduce(const void* attn, const int64_t attn_strides[2],
                            const void* w_o, const int64_t w_strides[2], void* out,

@@ -4,7 +4,7 @@
 // reference walks the pages of sequence row seq[t] through the block table, masks keys at
 // positions >= positions[t] + 1, and runs an fp32 online softmax over q.k * sm_scale.
 //
-// B200 design (one persistent wave, balanced by KV bytes, not by tokens):
+// B200 design (one wave of CTAs, balanced by KV bytes, not by tokens):
 //  * Work unit = one 16-token page of one (token, KV-head block).  A prologue scan over
 //    the query tokens gives the total U; CTA c owns units [c*chunk, (c+1)*chunk), so every
 //    CTA streams the same number of pages however ragged the contexts are.
