@@ -21,8 +21,8 @@
 //    split-K merge kernel chained after this one (programmatic dependent launch) folds into
 //    bf16 outputs.  No CTA ever waits for another.
 //  * Two CTA shapes.  Decode-only launches: two consumer warps per KV head, 3-4 CTAs per SM
-//    on every SM.  Launches followed by chunked-prefill tiles: the wide CTA (six consumer
-//    warps per KV head, an 8-16 stage ring, one CTA per SM) on only as many SMs as the decode
+//    on every SM.  Launches followed by chunked-prefill tiles: the wide CTA (five consumer
+//    warps per KV head, a 9-18 stage ring, one CTA per SM) on only as many SMs as the decode
 //    rows need (~1.3 MB of K/V each, a quarter to three quarters of the SMs); the others
 //    exit after the prologue, so the prefill tiles, which fill a whole SM per CTA, start on
 //    them while the decode rows stream.
@@ -40,7 +40,11 @@ namespace ss {
 namespace {
 
 constexpr int kMinChunk = 4;  // pages: lower bound on a CTA's share (limits tiny splits)
-constexpr int kWidePR = 6;    // consumer warps per KV head of the wide configuration
+// Consumer warps per KV head of the wide configuration.  A warp holds its stage while it
+// computes the page, so the ring keeps (stages - warps per head) pages in flight: 5 warps
+// with 9 stages measured best (6 with 8: a decode-heavy mixed step 146.9 us against 140.0;
+// 4 with 10: 147.6).
+constexpr int kWidePR = 5;
 // Bytes of K/V a wide CTA streams when the decode rows are few: the active wide CTAs are
 // sized so (between a quarter and three quarters of the SMs, the rest exit at once and
 // leave their SMs to the prefill tiles).  ~90 CTAs saturate HBM.
@@ -81,7 +85,7 @@ struct Traits {
   static constexpr int kThreads = 32 * (kNCW + 1);
   static constexpr int kMinBlocks = PR > 2 ? 1 : (KVB == 2 ? 3 : 4);  // CTAs per SM
   static constexpr int kSlab = kPage * KVB * HD * 2;   // one page of K (or V), KVB heads
-  static constexpr int kStages = PR > 2 ? (KVB == 2 ? 8 : 16) : (KVB == 2 ? 3 : 5);
+  static constexpr int kStages = PR > 2 ? (KVB == 2 ? 9 : 18) : (KVB == 2 ? 3 : 5);
   static constexpr int kStageBytes = 2 * kSlab;
   static constexpr int kRows = 16 * KVB;  // query-head rows per partial slot
   static constexpr int kSlotFloats = kRows * (HD + 2);
