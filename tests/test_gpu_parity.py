@@ -370,8 +370,13 @@ def test_prefill_work_queue_spans_more_items_than_sms(dev):
     assert K.device_errors(dev) == 0
 
 
-@pytest.mark.parametrize("seq_dtype,pos_dtype", [(torch.int32, torch.int64), (torch.int64, torch.int32)])
-def test_mixed_batch_index_arrays_staged_or_not_give_identical_results(dev, seq_dtype, pos_dtype):
+@pytest.mark.parametrize("seq_dtype,pos_dtype,H,KVH", [
+    (torch.int32, torch.int64, 16, 2),
+    (torch.int64, torch.int32, 16, 2),
+    (torch.int32, torch.int64, 8, 1),   # TP2 per-rank heads: the one-KV-head wide shape
+])
+def test_mixed_batch_index_arrays_staged_or_not_give_identical_results(dev, seq_dtype, pos_dtype,
+                                                                       H, KVH):
     """The wide decode shape next to the prefill tiles copies 16-byte aligned sequence-id and
     position arrays into shared memory for its scan, and scans them from global memory
     otherwise.  The same batch with the arrays as offset views (not 16-byte aligned) must give
@@ -381,7 +386,7 @@ def test_mixed_batch_index_arrays_staged_or_not_give_identical_results(dev, seq_
     g = torch.Generator().manual_seed(41)
     decode = [(int(c) - 1, 1) for c in torch.randint(256, 4097, (24,), generator=g)]
     prefill = [(int(c), 512) for c in torch.randint(0, 2049, (3,), generator=g)]
-    b = ragged_batch(decode + prefill, 16, 2, 128, seed=41, device=dev)
+    b = ragged_batch(decode + prefill, H, KVH, 128, seed=41, device=dev)
     seq = b.seq_ids.to(seq_dtype)
     pos = b.positions.to(pos_dtype)
     args = (b.q, b.k_pool, b.v_pool, b.block_tables)
