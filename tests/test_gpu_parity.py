@@ -401,3 +401,17 @@ def test_mixed_batch_index_arrays_staged_or_not_give_identical_results(dev, seq_
     offset = sb.ragged_attention_direct(*args, seq_off, pos_off, 128 ** -0.5)
     assert torch.equal(aligned, offset)
     assert K.device_errors(dev) == 0
+
+
+@pytest.mark.parametrize("rows,H,KVH", [
+    ([(5, 2)], 16, 2),                       # one run of two query tokens, nothing else
+    ([(100, 40), (0, 7), (300, 33)], 16, 2),  # prefill runs only: no decode row at all
+    ([(1000, 64)], 8, 1),                    # TP2 heads, one chunk
+])
+def test_prefill_only_launches_against_oracle(dev, rows, H, KVH):
+    """Launches whose every token belongs to a prefill run: the decode kernel beside the tiles
+    finds no units, and every one of its CTAs leaves right after its prologue."""
+    out, ref, path = _ragged_rows_case(dev, rows, H, KVH, seed=51)
+    assert path == 3
+    check_close(out, ref)
+    assert K.device_errors(dev) == 0
