@@ -33,7 +33,7 @@ def _bf16_f32(bits: np.ndarray) -> np.ndarray:
 
 # name -> spec.  seqs: (cached context before this step, query tokens this step).
 CASES = {
-    # contexts {17, 64, 200, 511}, one query token each, Qwen2.5-3B
+    # The reference's CPU-runnable decode case: contexts {17, 64, 200, 511}, one query token each, Qwen2.5-3B
     # geometry, 64-page pool, tables from a seeded permutation of page ids.
     "config1_decode": dict(H=16, KVH=2, D=128, seqs=[(16, 1), (63, 1), (199, 1), (510, 1)],
                            pages=64, scratch=0, padding=0, seed=1101),
