@@ -424,7 +424,7 @@ def run_decode64(args, rank, world, dist, h):
         "hbm_tbs": achieved / 1e3,
         "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
                      "frac": achieved / peak, "traffic": traffic_from_profile(),
-                     "kernel": "decode_attention_kernel<128,2,1> + merge_partials_kernel<128,2>",
+                     "kernel": "decode_attention_kernel<128,2,1,2> + merge_partials_kernel<128,2>",
                      "kernel_us": kernel_ms * 1e3,
                      "kernel_us_kind": "average interval of back-to-back attention calls "
                                        "(CUDA events around one graph of 100 calls)",

@@ -415,3 +415,20 @@ def test_prefill_only_launches_against_oracle(dev, rows, H, KVH):
     assert path == 3
     check_close(out, ref)
     assert K.device_errors(dev) == 0
+
+
+@pytest.mark.parametrize("chunks", [
+    40,   # 20,508 tokens, 641 windows: ranked longest first, straddling windows not split
+    70,   # 35,868 tokens, 1,121 windows: more windows than the ranking holds, taken in order
+])
+def test_prefill_tiles_beyond_the_ranked_window_limits(dev, chunks):
+    """Batches with more 32-token windows than the tile kernel's longest-first ranking splits
+    (512) or ranks at all (1024).  The decode rows come first, so every chunk starts inside a
+    window and windows straddle two chunks."""
+    g = torch.Generator().manual_seed(61 + chunks)
+    decode = [(int(c) - 1, 1) for c in torch.randint(64, 1025, (28,), generator=g)]
+    prefill = [(int(c), 512) for c in torch.randint(0, 301, (chunks,), generator=g)]
+    out, ref, path = _ragged_rows_case(dev, decode + prefill, 16, 2, seed=61 + chunks)
+    assert path == 3
+    check_close(out, ref)
+    assert K.device_errors(dev) == 0
