@@ -111,6 +111,15 @@ class ClockSampler:
 
     def __init__(self, index):
         self.index = index
+        self.gpu_id = str(index)
+        try:  # the UUID names the same GPU for nvidia-smi however CUDA numbers the devices
+            import torch
+
+            uuid = str(torch.cuda.get_device_properties(index).uuid)
+            if uuid:
+                self.gpu_id = uuid if uuid.startswith("GPU-") else "GPU-" + uuid
+        except (AttributeError, RuntimeError, AssertionError):
+            pass
         self.samples = []
         self.proc = None
         self.thread = None
@@ -118,7 +127,7 @@ class ClockSampler:
     def start(self):
         try:
             self.proc = subprocess.Popen(
-                ["nvidia-smi", f"--id={self.index}", f"--query-gpu={self.FIELDS}",
+                ["nvidia-smi", f"--id={self.gpu_id}", f"--query-gpu={self.FIELDS}",
                  "--format=csv,noheader,nounits", "-lms", "20"],
                 stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
         except OSError:
