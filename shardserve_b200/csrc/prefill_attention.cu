@@ -105,7 +105,9 @@ struct CtlP {
   int seg_keys[kMaxSeg];   // keys the segment's last row attends (max position + 1, clamped)
 };
 constexpr int kOffSort = (kOffCtlP + static_cast<int>(sizeof(CtlP)) + 15) / 16 * 16;
-constexpr int kSmemP = kOffSort + 2 * 4 * kMaxWinSort + 1024;  // + window cost and order
+constexpr int kCostBins = 1024;                // counting-sort bins (cost -1 .. 1022, clamped)
+constexpr int kOffHist = kOffSort + 2 * 4 * kMaxWinSort;  // after the window cost and order
+constexpr int kSmemP = kOffHist + 4 * kCostBins + 1024;
 
 // 2^x for a pair of fp32 values on the FMA pipe, offloading the MUFU unit (which computes
 // 16 exponentials per clock per SM, as many as the tensor core needs here at full rate).
@@ -163,6 +165,7 @@ __global__ void __launch_bounds__(kThreadsP, 1)
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   int* wcost = reinterpret_cast<int*>(smem + kOffSort);
   int* worder = wcost + kMaxWinSort;
+  int* hist = reinterpret_cast<int*>(smem + kOffHist);
   unsigned* sched = a.err + kSchedWord;
   const int nwin = static_cast<int>((a.T + kTQ - 1) / kTQ);
   const bool ranked = nwin <= kMaxWinSort;
@@ -173,6 +176,9 @@ __global__ void __launch_bounds__(kThreadsP, 1)
   // one; entry 2w + 1: the last segment, or absent (cost -1).
   const bool split = 2 * nwin <= kMaxWinSort;
   const int nent = split ? 2 * nwin : nwin;
+  // This CTA's first work item is taken from the counter now; its round trip overlaps the
+  // set-up and ranking below (CTAs that start earlier still take earlier, longer items).
+  const int first_item = tid == 0 ? static_cast<int>(atomicAdd(sched, 1u)) : 0;
 
   if (tid == 0) {
     mbar_init(bar(kBarQ), 1);
@@ -207,6 +213,7 @@ __global__ void __launch_bounds__(kThreadsP, 1)
     auto blocks_of = [&](long long keys) {
       return static_cast<int>((min(max(keys, 0ll), a.W * kPage) + kNB - 1) / kNB);
     };
+    for (int b = tid; b < kCostBins; b += kThreadsP) hist[b] = 0;
     for (int w = tid; w < nwin; w += kThreadsP) {
       const long long ts = static_cast<long long>(w) * kTQ, te = min(ts + kTQ - 1, a.T - 1);
       const long long s0 = seq_at(ts - 1), s1 = seq_at(ts), s2 = seq_at(ts + 1);
@@ -223,16 +230,48 @@ __global__ void __launch_bounds__(kThreadsP, 1)
         wcost[w] = c_first + c_last;
       }
     }
+    // Rank = entries of higher cost + entries of equal cost and lower index (highest cost
+    // first, ties by index), by a stable counting sort in linear work: a histogram of the
+    // costs (bin = cost + 1, so absent entries fall in bin 0 and rank last; costs above 1022
+    // share the top bin), an exclusive scan from the top bin down, then one warp places the
+    // entries in index order, 32 at a time.  (Counting each entry's rank over all entries
+    // costs ~5 instructions per pair: ~7 us per CTA at 1,024 entries.)
     __syncthreads();
-    for (int e = tid; e < nent; e += kThreadsP) {
-      const int c = wcost[e];
-      int rank = 0;
-      for (int v = 0; v < nent; ++v) {
-        const int cv = wcost[v];
-        rank += (cv > c) || (cv == c && v < e);
+    {
+      auto bin_of = [&](int c) { return min(c, kCostBins - 2) + 1; };
+      for (int e = tid; e < nent; e += kThreadsP) atomicAdd(&hist[bin_of(wcost[e])], 1);
+      __syncthreads();
+      if (warp == 0) {
+        int local = 0;  // lane l scans bins 1023 - 32 l down to 992 - 32 l
+#pragma unroll 8
+        for (int i = 0; i < 32; ++i) local += hist[kCostBins - 1 - (lane * 32 + i)];
+        int incl = local;
+#pragma unroll
+        for (int o = 1; o < 32; o <<= 1) {
+          const int y = __shfl_up_sync(0xffffffffu, incl, o);
+          if (lane >= o) incl += y;
+        }
+        int run = incl - local;
+#pragma unroll 8
+        for (int i = 0; i < 32; ++i) {
+          const int b = kCostBins - 1 - (lane * 32 + i);
+          const int h = hist[b];
+          hist[b] = run;
+          run += h;
+        }
+        __syncwarp();
+        if (lane == 0) ctl->nsub = hist[0];  // entries above bin 0: the present ones
+        __syncwarp();
+        for (int base = 0; base < nent; base += 32) {
+          const int e = base + lane;
+          const int b = e < nent ? bin_of(wcost[e]) : -1;
+          const unsigned same = __match_any_sync(0xffffffffu, b);
+          if (e < nent) worder[hist[b] + __popc(same & ((1u << lane) - 1u))] = e;
+          __syncwarp();
+          if (e < nent && lane == __ffs(same) - 1) hist[b] += __popc(same);
+          __syncwarp();
+        }
       }
-      worder[rank] = e;
-      if (c >= 0) atomicAdd(&ctl->nsub, 1);
     }
   }
   tc_fence_before();
@@ -256,7 +295,7 @@ __global__ void __launch_bounds__(kThreadsP, 1)
   // barriers, so every thread takes the same decisions.
   int iter = 0;
   auto item_head = [&]() -> ItemInfo {
-    if (tid == 0) ctl->item[iter & 1] = static_cast<int>(atomicAdd(sched, 1u));
+    if (tid == 0) ctl->item[iter & 1] = iter == 0 ? first_item : static_cast<int>(atomicAdd(sched, 1u));
     named_bar_sync(1, kThreadsP);
     const int item = ctl->item[iter & 1];
     ++iter;
