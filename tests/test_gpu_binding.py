@@ -102,3 +102,46 @@ def test_workspace_is_shared_with_the_c_abi_error_reader(dev):
     ws = K.workspace_for(dev)
     assert ws is not None and ws.dtype == torch.uint8 and ws.device == dev
     assert K.device_errors(dev) == 0
+
+
+def test_plain_ctypes_binding_matches_the_torch_binding(dev):
+    """The minimal ctypes binding a maintainer would add beside the reference's kernel.py
+    (C ABI only, no torch extension) gives bit-identical output to the torch binding."""
+    import ctypes
+
+    from shardserve_b200.workloads import decode_batch
+
+    lib = ctypes.CDLL(_native.LIB_PATH)
+    lib.ss_last_error_message.restype = ctypes.c_char_p
+    I64 = ctypes.c_int64
+
+    def strides(t):
+        return (I64 * t.dim())(*t.stride())
+
+    def attention(q, kp, vp, tables, seqs, pos, scale, ws):
+        out = torch.empty_like(q)
+        rc = lib.ss_ragged_paged_attention(
+            ctypes.c_void_p(q.data_ptr()), strides(q), ctypes.c_void_p(kp.data_ptr()), strides(kp),
+            ctypes.c_void_p(vp.data_ptr()), strides(vp), ctypes.c_void_p(tables.data_ptr()),
+            strides(tables), I64(tables.shape[0]), I64(tables.shape[1]), 0,
+            ctypes.c_void_p(seqs.data_ptr()), 0, ctypes.c_void_p(pos.data_ptr()), 1,
+            ctypes.c_void_p(out.data_ptr()), strides(out), I64(q.shape[0]), q.shape[1],
+            kp.shape[2], q.shape[2], I64(kp.shape[0]), ctypes.c_float(scale),
+            ctypes.c_void_p(ws.data_ptr()), ctypes.c_size_t(ws.numel()),
+            ctypes.c_void_p(torch.cuda.current_stream().cuda_stream))
+        if rc:
+            raise RuntimeError(lib.ss_last_error_message().decode())
+        return out
+
+    b = decode_batch([300, 17, 2049, 64], 16, 2, 128, seed=71, device=dev)
+    sb.kv_append(b.k_pool, b.v_pool, b.k_new, b.v_new, b.slots)
+    need = ctypes.c_size_t()
+    assert lib.ss_attention_workspace_bytes(0, I64(4), 16, 2, 128, ctypes.byref(need)) == 0
+    ws = torch.zeros(need.value, dtype=torch.uint8, device=dev)
+    seqs = b.seq_ids.to(torch.int32)
+    pos = b.positions.to(torch.int64)
+    tables = b.block_tables.to(torch.int32)
+    via_ctypes = attention(b.q, b.k_pool, b.v_pool, tables, seqs, pos, 128 ** -0.5, ws)
+    via_torch = sb.ragged_attention_direct(b.q, b.k_pool, b.v_pool, tables, seqs, pos, 128 ** -0.5)
+    torch.cuda.synchronize()
+    assert torch.equal(via_ctypes, via_torch)
