@@ -47,6 +47,7 @@ struct DecodeArgs {
   int G;         // CTAs in the grid
   int min_run;   // see token_in_long_run(); 0 = this launch owns every token
   int lo_ctas;   // wide shape: fewest CTAs that share the decode units (a quarter of the SMs)
+  int wide_per;  // wide shape: decode units (pages) per active CTA
   int4* desc;    // [T * nkvblk] split descriptor per row: {parts (0 none, 1 whole), first
                  // CTA, first part in the CTA's second slot, 0}; rewritten every call
   float* part;   // [2 * G] partial-state slots
@@ -125,10 +126,12 @@ struct DecodeGeometry {
 // one-CTA-per-SM configuration on half of the SMs when the layout has it.
 bool decode_geometry(int device, long long tokens, int heads, int kv_heads, int head_dim,
                      bool wide, DecodeGeometry* g, const char** why);
-// Wide shape: the grid for a launch whose block table has `rows` x `cols` entries (an upper
-// bound of its decode pages), between a quarter and three quarters of the SMs; sets g->G and
-// returns the lower bound the kernel keeps (DecodeArgs::lo_ctas).
-int wide_grid(DecodeGeometry* g, int device, long long rows, long long cols);
+// Wide shape: the grid for a launch of `tokens` query tokens whose block table has `rows` x
+// `cols` entries (an upper bound of its decode pages), between a quarter and three quarters
+// of the SMs; sets g->G and *per (DecodeArgs::wide_per) and returns the lower bound the
+// kernel keeps (DecodeArgs::lo_ctas).
+int wide_grid(DecodeGeometry* g, int device, long long rows, long long cols, long long tokens,
+              int* per);
 
 // Launches the TMA split-K decode kernel; returns a cudaError_t.
 cudaError_t launch_decode(const DecodeGeometry& g, const CUtensorMap& tmK, const CUtensorMap& tmV,

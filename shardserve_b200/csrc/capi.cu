@@ -515,7 +515,8 @@ int ss_ragged_paged_attention(const void* q, const int64_t q_strides[3], const v
       d.nkvblk = g.nkvblk;
       d.min_run = prefill ? ss::prefill_min_run() : 0;
       d.lo_ctas = g.G;
-      if (g.pr > 2) d.lo_ctas = ss::wide_grid(&g, device, bt_rows, bt_cols);
+      d.wide_per = 1;
+      if (g.pr > 2) d.lo_ctas = ss::wide_grid(&g, device, bt_rows, bt_cols, tokens, &d.wide_per);
       d.G = g.G;
       uint8_t* ws = static_cast<uint8_t*>(workspace);
       d.part = reinterpret_cast<float*>(ws + ss::kWsHeader);

@@ -30,6 +30,7 @@
 #include <math_constants.h>
 
 #include <algorithm>
+#include <cmath>
 #include <mutex>
 
 #include "attention.cuh"
@@ -45,10 +46,16 @@ constexpr int kMinChunk = 4;  // pages: lower bound on a CTA's share (limits tin
 // with 9 stages measured best (6 with 8: a decode-heavy mixed step 146.9 us against 140.0;
 // 4 with 10: 147.6).
 constexpr int kWidePR = 5;
-// Bytes of K/V a wide CTA streams when the decode rows are few: the active wide CTAs are
-// sized so (between a quarter and three quarters of the SMs, the rest exit at once and
-// leave their SMs to the prefill tiles).  ~90 CTAs saturate HBM.
+// Bytes of K/V a wide CTA streams beside at most kWideBaseTokens prefill tokens: the active
+// wide CTAs are sized so (between a quarter and three quarters of the SMs; the rest exit at
+// once and leave their SMs to the prefill tiles).  ~90 CTAs saturate HBM.  With more prefill
+// tokens the tiles need more of the SMs, and the share grows as (tokens / 1024)^0.4.
+// Measured (graph-replayed steps, 56 decode rows + 512-token chunks, fixed 1.3 / 1.7 / 2.2 /
+// 3.0 MB per CTA): 2 chunks 53.5 / 61.8 / 71.3 / 86.3 us, 4 chunks 73.1 / 68.1 / 76.6 / 92.0,
+// 8 chunks 105.6 / 100.2 / 101.3 / 107.2, 16 chunks 170.9 / 165.6 / 165.7 / 158.9.
 constexpr long long kWideBytesPerCta = 1344LL << 10;
+constexpr double kWideBaseTokens = 1024.0;
+constexpr double kWideTokenExp = 0.4;
 
 enum : int { kFirst = 1, kLast = 2, kWhole = 4, kDone = 8, kFirstPartLate = 16 };
 
@@ -323,7 +330,7 @@ __global__ void __launch_bounds__(Traits<HD, KVB, NG, PR>::kThreads, Traits<HD, 
         s += u > 0 ? u : 0;
       }
       long long start = block_excl_scan<NT>(s, ctl, U);
-      const long long per_cta = max(1LL, kWideBytesPerCta / (2 * Tr::kSlab));
+      const long long per_cta = max(1, d.wide_per);
       const long long ctas = min(static_cast<long long>(d.G),
                                  max(static_cast<long long>(d.lo_ctas), (U + per_cta - 1) / per_cta));
       chunk = max((U + ctas - 1) / ctas, static_cast<long long>(kMinChunk));
@@ -383,7 +390,7 @@ __global__ void __launch_bounds__(Traits<HD, KVB, NG, PR>::kThreads, Traits<HD, 
     if (a.T <= CH) U = total;  // single pass: the scan also gives the total
     long long ctas = d.G;  // CTAs that share the units
     if (PR > 2) {
-      const long long per = max(1LL, kWideBytesPerCta / (2 * Tr::kSlab));
+      const long long per = max(1, d.wide_per);
       ctas = min(static_cast<long long>(d.G), max(static_cast<long long>(d.lo_ctas), (U + per - 1) / per));
     }
     chunk = max((U + ctas - 1) / ctas, static_cast<long long>(kMinChunk));
@@ -1117,11 +1124,18 @@ bool geometry_ng(int device, long long tokens, int kv_heads, int group, bool wid
 
 }  // namespace
 
-int wide_grid(DecodeGeometry* g, int device, long long rows, long long cols) {
+int wide_grid(DecodeGeometry* g, int device, long long rows, long long cols, long long tokens,
+              int* per_out) {
   const int sms = sm_count(device);
   const int lo = std::max(1, sms / 4), hi = std::max(lo, 3 * sms / 4);
   const long long slab = static_cast<long long>(kPage) * g->kvb * 128 * 2;
-  const long long per = std::max(1LL, kWideBytesPerCta / (2 * slab));
+  // Prefill tokens, about: every token beyond one per block-table row.
+  const double pre = static_cast<double>(std::max(0LL, tokens - rows));
+  const double scale = std::pow(std::max(1.0, pre / kWideBaseTokens), kWideTokenExp);
+  const long long per = std::max(
+      1LL, std::min<long long>(1LL << 30,
+                               static_cast<long long>(scale * (kWideBytesPerCta / (2 * slab)))));
+  *per_out = static_cast<int>(per);
   const long long bound = rows * cols * g->nkvblk;  // decode pages at most
   g->G = static_cast<int>(std::min<long long>(hi, std::max<long long>(lo, (bound + per - 1) / per)));
   return lo;
