@@ -6,6 +6,12 @@ heads, head_dim 128, scale 1/sqrt(128)), page size 16, pool = total pages x 1.1 
 pages, block tables scattered by a seeded permutation, bf16 N(0,1) data.  One step = append
 the step's new K/V rows (Cache.write) + ragged_attention_direct over the batch.
 
+The default run also measures the other configurations and attaches them to the same JSON
+line under "workloads" (each with its own steps, step time, roofline fraction and clocks):
+the mixed chunked-prefill batch, its prefill rows alone, one 36-layer decode step, the
+long-context TP2 layout and, on 2+ GPUs, the TP2 o_proj + all-reduce (`--no-extras` skips
+them).
+
 Other workloads (`--workload`, one JSON line each; same timing rules):
   mixed     8 prefill chunks x 512 tokens on cached context U[0, 2048] (causal inside the
             chunk) + 56 decode rows with context U[256, 4096], one ragged launch per step
@@ -66,8 +72,8 @@ def parse():
     p.add_argument("--warmup", type=int, default=200)
     p.add_argument("--impl", choices=["ours", "reference"], default="ours")
     p.add_argument("--workload",
-                   choices=["decode64", "mixed", "layers36", "tp2long", "rope", "metadata",
-                            "tp2oproj"],
+                   choices=["decode64", "mixed", "prefill_only", "layers36", "tp2long", "rope",
+                            "metadata", "tp2oproj"],
                    default="decode64")
     p.add_argument("--replicas", type=int, default=4, help="batches rotated to defeat L2")
     p.add_argument("--graph-steps", type=int, default=100, help="steps per captured graph")
@@ -75,6 +81,12 @@ def parse():
     p.add_argument("--cpu-seconds", type=float, default=10.0)
     p.add_argument("--pool-frac", type=float, default=0.6, help="tp2long pool share of HBM")
     p.add_argument("--seed", type=int, default=2024)
+    p.add_argument("--no-extras", action="store_true",
+                   help="decode64: skip the other configurations attached to the line")
+    p.add_argument("--extra-steps", type=int, default=40,
+                   help="timed steps of each attached configuration (36-layer steps: / 8)")
+    p.add_argument("--soak", type=float, default=0.25,
+                   help="seconds of the same replays after a timed region, for clock samples")
     return p.parse_args()
 
 
@@ -103,75 +115,180 @@ def peaks():
 
 
 class ClockSampler:
-    """Samples nvidia-smi SM clocks and throttle reasons every 20 ms (read-only queries)."""
+    """Samples the GPU's SM clock, power and clock-event (throttle) reasons in a background
+    thread: NVML every millisecond (read-only queries), else `nvidia-smi -lms 20`.
+
+    `summary(t0, t1, soak)` reports the samples taken inside the timed region [t0, t1]
+    (host monotonic clock) and, separately, those of the soak window that follows it (the
+    same graph replays, untimed): a region of a few hundred microseconds holds at most a
+    sample or two, so the soak window characterises the clocks the region ran at."""
 
     FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
               "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
               "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+    # NVML clock-event reason bits (nvmlClocksEventReason*).
+    REASONS = ((0x4, "sw_power_cap"), (0x8, "hw_slowdown"), (0x20, "sw_thermal_slowdown"),
+               (0x40, "hw_thermal_slowdown"), (0x80, "hw_power_brake_slowdown"))
 
     def __init__(self, index):
         self.index = index
-        self.gpu_id = str(index)
-        try:  # the UUID names the same GPU for nvidia-smi however CUDA numbers the devices
+        self.uuid = None
+        try:  # the UUID names the same GPU for NVML however CUDA numbers the devices
             import torch
 
             uuid = str(torch.cuda.get_device_properties(index).uuid)
             if uuid:
-                self.gpu_id = uuid if uuid.startswith("GPU-") else "GPU-" + uuid
+                self.uuid = uuid if uuid.startswith("GPU-") else "GPU-" + uuid
         except (AttributeError, RuntimeError, AssertionError):
             pass
-        self.samples = []
+        self.samples = []  # (monotonic s, sm MHz, max sm MHz, power W, [reason names])
+        self.source = None
         self.proc = None
         self.thread = None
+        self._stop = threading.Event()
 
     def start(self):
         try:
+            import pynvml
+
+            pynvml.nvmlInit()
+            h = (pynvml.nvmlDeviceGetHandleByUUID(self.uuid) if self.uuid
+                 else pynvml.nvmlDeviceGetHandleByIndex(self.index))
+            mx = pynvml.nvmlDeviceGetMaxClockInfo(h, pynvml.NVML_CLOCK_SM)
+            self.source = "nvml, 1 ms"
+            self.thread = threading.Thread(target=self._poll_nvml, args=(pynvml, h, mx),
+                                           daemon=True)
+            self.thread.start()
+            return
+        except Exception:  # noqa: BLE001 - any NVML problem: fall back to nvidia-smi
+            pass
+        try:
+            gpu_id = self.uuid or str(self.index)
             self.proc = subprocess.Popen(
-                ["nvidia-smi", f"--id={self.gpu_id}", f"--query-gpu={self.FIELDS}",
+                ["nvidia-smi", f"--id={gpu_id}", f"--query-gpu={self.FIELDS}",
                  "--format=csv,noheader,nounits", "-lms", "20"],
                 stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
         except OSError:
             return
-        self.thread = threading.Thread(target=self._read, daemon=True)
+        self.source = "nvidia-smi, 20 ms"
+        self.thread = threading.Thread(target=self._read_smi, daemon=True)
         self.thread.start()
 
-    def _read(self):
+    def _poll_nvml(self, nv, h, mx):
+        get_reasons = getattr(nv, "nvmlDeviceGetCurrentClocksEventReasons",
+                              getattr(nv, "nvmlDeviceGetCurrentClocksThrottleReasons", None))
+        while not self._stop.is_set():
+            try:
+                sm = nv.nvmlDeviceGetClockInfo(h, nv.NVML_CLOCK_SM)
+                pw = nv.nvmlDeviceGetPowerUsage(h) / 1000.0
+                bits = get_reasons(h) if get_reasons else 0
+            except Exception:  # noqa: BLE001
+                break
+            names = [n for b, n in self.REASONS if bits & b]
+            self.samples.append((time.monotonic(), float(sm), float(mx), pw, names))
+            time.sleep(0.001)
+
+    def _read_smi(self):
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
         for line in self.proc.stdout:
-            self.samples.append((time.monotonic(), line.strip()))
+            parts = [x.strip() for x in line.split(",")]
+            if len(parts) < 9:
+                continue
+            try:
+                sm, mx = float(parts[1]), float(parts[2])
+                pw = float(parts[3])
+            except ValueError:
+                continue
+            self.samples.append((time.monotonic(), sm, mx, pw,
+                                 [names[i] for i in range(4) if parts[5 + i] == "Active"]))
 
     def stop(self):
+        self._stop.set()
         if self.proc:
             self.proc.terminate()
             try:
                 self.proc.wait(timeout=5)
             except subprocess.TimeoutExpired:
                 self.proc.kill()
+        if self.thread:
+            self.thread.join(timeout=5)
 
-    def summary(self, t0, t1):
-        rows = []
-        for ts, line in self.samples:
-            parts = [x.strip() for x in line.split(",")]
-            if len(parts) < 9:
-                continue
-            try:
-                rows.append((ts, float(parts[1]), float(parts[2]), parts))
-            except ValueError:
-                continue
-        inside = [r for r in rows if t0 <= r[0] <= t1]
-        use = inside or rows
-        if not use:
-            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["no samples"], "samples": 0}
-        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
-        reasons = sorted({names[i] for r in use for i in range(4) if r[3][5 + i] == "Active"})
-        return {"sm_mhz": statistics.median(r[1] for r in use), "sm_max_mhz": max(r[2] for r in use),
-                "reasons": reasons, "samples": len(inside), "samples_outside_region": len(rows) - len(inside)}
+    @staticmethod
+    def _stats(rows):
+        if not rows:
+            return None
+        return {"sm_mhz": statistics.median(r[1] for r in rows),
+                "sm_mhz_min": min(r[1] for r in rows), "sm_max_mhz": max(r[2] for r in rows),
+                "power_w_max": max(r[3] for r in rows),
+                "reasons": sorted({n for r in rows for n in r[4]}), "samples": len(rows)}
+
+    def summary(self, t0, t1, soak=None):
+        """Clocks of the timed region [t0, t1] (and of the soak window after it)."""
+        inside = self._stats([r for r in self.samples if t0 <= r[0] <= t1])
+        after = self._stats([r for r in self.samples if soak and soak[0] <= r[0] <= soak[1]])
+        head = inside or after
+        if head is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["no samples"], "samples": 0,
+                    "source": self.source}
+        out = {"sm_mhz": head["sm_mhz"], "sm_max_mhz": head["sm_max_mhz"],
+               "reasons": sorted(set((inside or {}).get("reasons", []))
+                                 | set((after or {}).get("reasons", []))),
+               "samples": inside["samples"] if inside else 0,
+               "from": "timed region" if inside else "soak after the timed region",
+               "source": self.source}
+        if after:
+            out["soak"] = dict(after, seconds=round(soak[1] - soak[0], 3))
+        if inside:
+            out["region"] = inside
+        return out
 
 
 # ---------------------------------------------------------------------------------------
+def reference_cache_class():
+    """The reference's own Cache (shardserve/cache.py:37-61) from its unmodified offline
+    install in baseline/_ref (or SHARDSERVE_REFERENCE); None where it is absent."""
+    for path in (os.environ.get("SHARDSERVE_REFERENCE"), os.path.join(ROOT, "baseline", "_ref")):
+        if path and os.path.isdir(os.path.join(path, "shardserve")) and path not in sys.path:
+            sys.path.append(path)
+    try:
+        from shardserve.cache import Cache
+    except ImportError:
+        return None
+    return Cache
+
+
+class ReferenceCpuPath:
+    """The reference's CPU attention path, unchanged: Cache.write (cache.py:47-49) of the
+    step's new K/V rows, then Cache.diagnostic (cache.py:51-61) over the step's query tokens,
+    on the batch-64 workload's synthetic data, in `dtype` (bf16: the reference's pool dtype)."""
+
+    def __init__(self, cache_cls, lengths, seed, dtype):
+        import torch
+
+        b = _cpu_batch(lengths, seed)
+        c = dict(num_hidden_layers=1, num_key_value_heads=KV_HEADS,
+                 hidden_size=HEADS * HEAD_DIM, num_attention_heads=HEADS)
+        n_pages = b["kp"].shape[0]
+        self.cache = cache_cls(c, 1, n_pages - 8, "cpu", dtype)
+        self.cache.k[0].copy_(torch.from_numpy(b["kp"]))
+        self.cache.v[0].copy_(torch.from_numpy(b["vp"]))
+        t = lambda x: torch.from_numpy(x)
+        self.q = t(b["q"]).to(dtype)
+        self.k_new, self.v_new = t(b["kn"]).to(dtype), t(b["vn"]).to(dtype)
+        self.slots = t(b["slots"])
+        self.tables, self.seqs, self.pos = t(b["bt"]), t(b["seq"]), t(b["pos"])
+        self.n = len(lengths)
+
+    def step(self, sel=None):
+        idx = slice(None) if sel is None else sel
+        self.cache.write(0, self.k_new[idx], self.v_new[idx], self.slots[idx])
+        return self.cache.diagnostic(0, self.q[idx], self.tables, self.seqs[idx], self.pos[idx])
+
+
 def run_reference(args, rank, world):
-    """Reference arm: the CPU restatement of the reference attention path (the reference is
-    Python/PyTorch/Triton and its CPU path cannot travel here), timed on this host's cores,
-    rank 0 only."""
+    """Reference arm: the reference's own CPU path (Cache.write + Cache.diagnostic from its
+    unmodified install) on this arm's batch-64 workload, on all host threads, rank 0 only.
+    Without the install, the CPU restatement (numpy oracle) of the same path."""
     if rank != 0:
         return
     import numpy as np
@@ -182,21 +299,38 @@ def run_reference(args, rank, world):
     threads = oracle.host_threads()
     torch.set_num_threads(threads)
     lengths = rank_lengths(world, 0, args.seed)
-    b = _cpu_batch(lengths, args.seed)
-    # A step is one decode token per host thread, fewer when K + W steps of that size would
-    # not finish in about two minutes (the arm must end within a few minutes for any K).
-    t0 = time.perf_counter()
-    oracle.ragged_attention(b["q"][:1], b["kp"], b["vp"], b["bt"][:1], np.zeros(1, np.int32),
-                            b["pos"][:1], SCALE)
-    t_tok = time.perf_counter() - t0
-    budget = 120.0 / max(1, args.steps + args.warmup)
-    per_step = int(max(1, min(threads, len(lengths), budget / max(t_tok, 1e-6))))
+    n = len(lengths)
+    cache_cls = reference_cache_class()
+    if cache_cls is not None:
+        kind = "reference"
+        path = ReferenceCpuPath(cache_cls, lengths, args.seed, torch.bfloat16)
+        t0 = time.perf_counter()
+        path.step()
+        t_step = time.perf_counter() - t0
+        # A step is the whole batch when K + W such steps end within ~2.5 minutes, else a
+        # rotating slice of it.
+        per_step = int(max(1, min(n, n * 150.0 / max(1, args.steps + args.warmup) / t_step)))
 
-    def step(i):
-        sel = [(i * per_step + j) % len(lengths) for j in range(per_step)]
-        oracle.kv_append(b["kp"], b["vp"], b["kn"][sel], b["vn"][sel], b["slots"][sel])
-        oracle.ragged_attention(b["q"][sel], b["kp"], b["vp"], b["bt"], b["seq"][sel],
-                                b["pos"][sel], SCALE, threads=per_step)
+        def step(i):
+            sel = torch.tensor([(i * per_step + j) % n for j in range(per_step)])
+            path.step(None if per_step == n else sel)
+        what = ("shardserve.cache.Cache.write + Cache.diagnostic from the reference's "
+                "unmodified install, bf16 pools (the reference's pool dtype)")
+    else:
+        kind = "port"
+        b = _cpu_batch(lengths, args.seed)
+        t0 = time.perf_counter()
+        oracle.ragged_attention(b["q"][:1], b["kp"], b["vp"], b["bt"][:1], np.zeros(1, np.int32),
+                                b["pos"][:1], SCALE)
+        t_tok = time.perf_counter() - t0
+        per_step = int(max(1, min(n, 150.0 / max(1, args.steps + args.warmup) / max(t_tok, 1e-6))))
+
+        def step(i):
+            sel = [(i * per_step + j) % n for j in range(per_step)]
+            oracle.kv_append(b["kp"], b["vp"], b["kn"][sel], b["vn"][sel], b["slots"][sel])
+            oracle.ragged_attention(b["q"][sel], b["kp"], b["vp"], b["bt"], b["seq"][sel],
+                                    b["pos"][sel], SCALE, threads=threads)
+        what = "numpy restatement of Cache.write + the attention path (reference not installed)"
 
     for i in range(args.warmup):
         step(i)
@@ -205,15 +339,16 @@ def run_reference(args, rank, world):
         step(args.warmup + i)
     dt = time.perf_counter() - t0
     value = args.steps * per_step / dt
-    sample = (f"{per_step} decode tokens per step (one per host thread), rotating over the "
-              f"{len(lengths)}-token batch; numpy port of Cache.write + the attention path")
+    sample = (f"{per_step} of the {n} decode tokens per step" if per_step < n else
+              f"all {n} decode tokens per step") + f"; {what}; {threads} host threads"
     line = {
         "impl": "reference", "metric": METRIC, "value": value, "unit": "tok/s",
         "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
         "ms_per_step": dt * 1e3 / args.steps, "higher_is_better": True, "scaling": "weak",
-        "vs_baseline": None, "dtype": "f32", "data": "synthetic",
-        "config": {"workload": WORKLOAD, "step": sample},
-        "cpu_baseline": {"value": value, "unit": "tok/s", "cores": per_step, "kind": "port",
+        "vs_baseline": None, "dtype": "bf16" if kind == "reference" else "f32",
+        "data": "synthetic",
+        "config": {"workload": WORKLOAD, "tokens_per_step": per_step},
+        "cpu_baseline": {"value": value, "unit": "tok/s", "cores": threads, "kind": kind,
                          "sample": sample},
         "e2e": {"value": value, "unit": "tok/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
@@ -245,22 +380,41 @@ def _cpu_batch(lengths, seed):
 
 
 def cpu_baseline(args, lengths):
-    """The oracle (numpy port of the reference path) on a bounded sample, all host threads."""
+    """The reference's own CPU path (Cache.write + Cache.diagnostic, bf16 pools, from its
+    unmodified install) on this rank's batch for ~cpu_seconds on all host threads; beside it
+    the numpy restatement (the oracle) for a few seconds.  Without the install, the port."""
+    import torch
+
     import oracle
 
     threads = oracle.host_threads()
+    torch.set_num_threads(threads)
     b = _cpu_batch(lengths, args.seed)
-    done = 0
-    t0 = time.perf_counter()
-    while time.perf_counter() - t0 < args.cpu_seconds:
+    done, t0 = 0, time.perf_counter()
+    budget = args.cpu_seconds / 2
+    while time.perf_counter() - t0 < budget:
         oracle.kv_append(b["kp"], b["vp"], b["kn"], b["vn"], b["slots"])
         oracle.ragged_attention(b["q"], b["kp"], b["vp"], b["bt"], b["seq"], b["pos"], SCALE,
                                 threads=threads)
         done += len(lengths)
     dt = time.perf_counter() - t0
-    return {"value": done / dt, "unit": "tok/s", "cores": threads, "kind": "port",
-            "sample": f"{done // len(lengths)} full passes over this rank's {len(lengths)}-token "
-                      f"batch in {dt:.1f} s (numpy, {threads} threads)"}
+    port = {"value": done / dt, "unit": "tok/s", "cores": threads, "kind": "port",
+            "sample": f"{done // len(lengths)} full passes over the {len(lengths)}-token batch "
+                      f"in {dt:.1f} s (numpy oracle, {threads} threads)"}
+    cache_cls = reference_cache_class()
+    if cache_cls is None:
+        return port
+    path = ReferenceCpuPath(cache_cls, lengths, args.seed, torch.bfloat16)
+    done, t0 = 0, time.perf_counter()
+    while time.perf_counter() - t0 < args.cpu_seconds:
+        path.step()
+        done += len(lengths)
+    dt = time.perf_counter() - t0
+    return {"value": done / dt, "unit": "tok/s", "cores": threads, "kind": "reference",
+            "sample": f"{done // len(lengths)} full passes over the {len(lengths)}-token batch in "
+                      f"{dt:.1f} s: shardserve.cache.Cache.write + Cache.diagnostic, unmodified, "
+                      f"bf16 pools, torch.get_num_threads() = {torch.get_num_threads()}",
+            "port": port}
 
 
 # ---------------------------------------------------------------------------------------
@@ -306,8 +460,24 @@ class Harness:
         torch.cuda.synchronize()
         return g
 
-    def run_steps(self, fns, k, warm):
-        """Runs `warm` untimed then exactly `k` timed steps; returns device ms of the k."""
+    def gather(self, x):
+        """x from every rank (a one-element list on one GPU)."""
+        if self.dist is None:
+            return [x]
+        t = self.torch.tensor([x], dtype=self.torch.float64, device=self.dev)
+        out = [self.torch.zeros_like(t) for _ in range(self.dist.get_world_size())]
+        self.dist.all_gather(out, t)
+        return [float(o.item()) for o in out]
+
+    def run_steps(self, fns, k, warm, soak_s=0.0):
+        """Runs `warm` untimed then exactly `k` timed steps; returns the device ms of the k,
+        the host-clock bounds of the timed region and of the soak that follows it.
+
+        Steps are replayed from CUDA graphs of S steps.  Every graph the timed region
+        replays is replayed once before it, so the region never pays a graph's first-replay
+        upload; then come the `warm` warm-up steps.  After the region (closed by barrier +
+        synchronize), the same graph is replayed for `soak_s` seconds, untimed, so the clock
+        sampler sees the clocks this load runs at."""
         torch = self.torch
         S = min(self.S, max(k, 1))
         full = self.capture(fns, S)
@@ -316,6 +486,9 @@ class Harness:
         warm_full, warm_rem = divmod(warm, S)
         warm_g = self.capture(fns, warm_rem) if warm_rem else None
         with torch.cuda.stream(self.stream):
+            full.replay()  # first replays (graph upload) outside the timed region
+            if rem_g is not None:
+                rem_g.replay()
             for _ in range(warm_full):
                 full.replay()
             if warm_g is not None:
@@ -332,7 +505,15 @@ class Harness:
             e1.record(self.stream)
         self.barrier()
         t1 = time.monotonic()
-        return e0.elapsed_time(e1), (t0, t1)
+        t2 = t1
+        if soak_s > 0:
+            with torch.cuda.stream(self.stream):
+                while time.monotonic() - t1 < soak_s:
+                    full.replay()
+                    self.stream.synchronize()
+            t2 = time.monotonic()
+        self.barrier()  # every rank leaves together (the soak length differs per rank)
+        return e0.elapsed_time(e1), (t0, t1), (t1, t2)
 
     def interval_ms(self, fns, n):
         """Mean device time per call of `n` calls captured back to back in one graph (fns
@@ -374,6 +555,22 @@ class Harness:
         return statistics.mean(a.elapsed_time(b) for a, b in ev)
 
 
+def launches_per_call(fn):
+    """Kernels of this library one call of `fn` enqueues (the library's own counter)."""
+    from shardserve_b200 import _native
+
+    lib = _native.lib()
+    before = lib.ss_kernel_launch_count()
+    fn()
+    return int(lib.ss_kernel_launch_count() - before)
+
+
+def rank_times(h, ms, steps):
+    """Per-rank step time (min / median / max over ranks), in ms."""
+    per = [x / steps for x in h.gather(ms)]
+    return {"min": min(per), "median": statistics.median(per), "max": max(per)}
+
+
 def run_decode64(args, rank, world, dist, h):
     import torch
 
@@ -399,7 +596,8 @@ def run_decode64(args, rank, world, dist, h):
         return lambda: sb.ragged_attention_direct(b.q, b.k_pool, b.v_pool, b.block_tables,
                                                   b.seq_ids, b.positions, SCALE)
 
-    for b in batches:
+    per_step = launches_per_call(step_fn(batches[0]))
+    for b in batches[1:]:
         step_fn(b)()
     torch.cuda.synchronize()
     assert K.last_attention_path() == 1, "attention did not take the TMA tensor-core path"
@@ -407,12 +605,13 @@ def run_decode64(args, rank, world, dist, h):
 
     clocks = ClockSampler(dev.index)
     clocks.start()
-    time.sleep(0.3)
+    time.sleep(0.05)
     steps = [step_fn(b) for b in batches]
-    ms, (t0, t1) = h.run_steps(steps, args.steps, args.warmup)
+    ms, (t0, t1), soak = h.run_steps(steps, args.steps, args.warmup, soak_s=args.soak)
     kernel_ms = h.interval_ms([attn_fn(b) for b in batches], min(args.graph_steps, 200))
     isolated_ms = h.per_launch_ms([attn_fn(b) for b in batches], min(args.graph_steps, 200))
     clocks.stop()
+    per_rank = rank_times(h, ms, args.steps)
     ms = h.max_over_ranks(ms)
     kernel_ms = h.max_over_ranks(kernel_ms)
     isolated_ms = h.max_over_ranks(isolated_ms)
@@ -422,6 +621,8 @@ def run_decode64(args, rank, world, dist, h):
     abytes = attention_bytes(lengths, HEADS, KV_HEADS, HEAD_DIM)
     peak, _, peak_kind = peaks()
     achieved = abytes / (kernel_ms / 1e3) / 1e9
+    del batches
+    torch.cuda.empty_cache()
     line = {
         "metric": METRIC, "value": value, "unit": "tok/s", "n_gpus": world, "steps": args.steps,
         "warmup": args.warmup, "ms_per_step": ms / args.steps, "higher_is_better": True,
@@ -429,7 +630,9 @@ def run_decode64(args, rank, world, dist, h):
         "config": {"workload": WORKLOAD, "tokens_per_gpu_step": T,
                    "parallelism": f"request-sharded x{world} (LPT by context), no collective",
                    "l2": f"{R} rotating batches of ~{abytes / 1e6:.0f} MB each per GPU (> L2)",
-                   "graph": f"{min(args.graph_steps, args.steps)} steps per CUDA graph"},
+                   "graph": f"{min(args.graph_steps, args.steps)} steps per CUDA graph, every "
+                            "graph replayed once before the timed region"},
+        "ms_per_step_per_rank": per_rank,
         "hbm_tbs": achieved / 1e3,
         "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
                      "frac": achieved / peak, "traffic": traffic_from_profile(),
@@ -438,29 +641,71 @@ def run_decode64(args, rank, world, dist, h):
                      "kernel_us_kind": "average interval of back-to-back attention calls "
                                        "(CUDA events around one graph of 100 calls)",
                      "kernel_us_isolated": isolated_ms * 1e3,
+                     "frac_isolated": abytes / (isolated_ms / 1e3) / 1e9 / peak,
                      "algorithmic_bytes": abytes,
                      "peak_kind": f"{peak_kind} copy bandwidth"},
         "append_bytes": append_bytes(T, KV_HEADS, HEAD_DIM),
         "e2e": e2e,
-        "gpu_launches": 3 * args.steps,
-        "clocks": clocks.summary(t0, t1),
+        "gpu_launches": per_step * args.steps,
+        "gpu_launches_per_step": per_step,
+        "clocks": clocks.summary(t0, t1, soak),
     }
+    if not args.no_extras:
+        line["workloads"] = run_extras(args, rank, world, dist, h)
     if rank == 0:
         line["cpu_baseline"] = cpu_baseline(args, lengths) if world == 1 else None
     return line
 
 
-def run_mixed(args, rank, world, dist, h):
+def run_extras(args, rank, world, dist, h):
+    """The other configurations, measured after the headline with reduced step counts; each
+    entry carries its own steps, step time, roofline fraction and clocks."""
+    import argparse as _ap
+
+    import torch
+
+    sub = _ap.Namespace(**vars(args))
+    sub.steps = max(3, args.extra_steps)
+    sub.warmup = max(3, min(args.warmup, 10))
+    sub.graph_steps = min(args.graph_steps, 20)
+    out = {}
+    runs = [("mixed", run_mixed), ("prefill_only", run_prefill_only),
+            ("layers36", run_layers36), ("tp2long", run_tp2long)]
+    if world >= 2 and world % 2 == 0:
+        runs.append(("tp2oproj", run_tp2oproj))
+    for name, fn in runs:
+        torch.cuda.empty_cache()
+        h.S = sub.graph_steps
+        try:
+            out[name] = fn(sub, rank, world, dist, h)
+        finally:
+            torch.cuda.empty_cache()
+    h.S = args.graph_steps
+    return out
+
+
+def _timed_with_clocks(args, h, fns, k, w):
+    clocks = ClockSampler(h.dev.index)
+    clocks.start()
+    ms, (t0, t1), soak = h.run_steps(fns, k, w, soak_s=args.soak)
+    clocks.stop()
+    per_rank = rank_times(h, ms, k)
+    return h.max_over_ranks(ms), per_rank, clocks.summary(t0, t1, soak)
+
+
+def run_mixed(args, rank, world, dist, h, prefill_only=False):
     """8 prefill chunks x 512 tokens on cached context U[0, 2048] + 56 decode rows with
     context U[256, 4096] (decode rows first, as the reference scheduler packs them)."""
     import torch
 
     import shardserve_b200 as sb
-    from shardserve_b200.workloads import attention_bytes, prefill_flops, ragged_batch
+    from shardserve_b200 import kernel as K
+    from shardserve_b200.workloads import (attention_bytes, mixed_rows, prefill_flops,
+                                           ragged_batch)
 
-    g = torch.Generator().manual_seed(args.seed + rank)
-    decode = [(int(c) - 1, 1) for c in torch.randint(256, 4097, (56,), generator=g)]
-    prefill = [(int(c), 512) for c in torch.randint(0, 2049, (8,), generator=g)]
+    decode, prefill = mixed_rows(args.seed + rank)
+    if prefill_only:
+        decode = []
     rows = decode + prefill
     R = max(1, args.replicas)
     batches = [ragged_batch(rows, HEADS, KV_HEADS, HEAD_DIM, seed=args.seed + 7 * r + rank,
@@ -474,23 +719,40 @@ def run_mixed(args, rank, world, dist, h):
                                        b.positions, SCALE)
         return f
 
-    for b in batches:
+    per_step = launches_per_call(step_fn(batches[0]))
+    for b in batches[1:]:
         step_fn(b)()
     torch.cuda.synchronize()
-    ms, (t0, t1) = h.run_steps([step_fn(b) for b in batches], args.steps, args.warmup)
-    ms = h.max_over_ranks(ms)
+    assert K.last_attention_path() == 3, "chunked-prefill rows did not take the tcgen05 tiles"
+    ms, per_rank, clk = _timed_with_clocks(args, h, [step_fn(b) for b in batches], args.steps,
+                                           args.warmup)
     step_s = ms / 1e3 / args.steps
     flops = prefill_flops(prefill, HEADS, HEAD_DIM)
-    dbytes = attention_bytes([c + n for c, n in decode], HEADS, KV_HEADS, HEAD_DIM)
+    dbytes = attention_bytes([c + n for c, n in decode], HEADS, KV_HEADS, HEAD_DIM) if decode else 0
     _, tflops_peak, kind = peaks()
-    return {"metric": "mixed chunked-prefill + decode query tok/s", "workload": "mixed",
+    achieved = flops / step_s / 1e12
+    del batches
+    return {"metric": ("prefill-only chunked-prefill" if prefill_only else
+                       "mixed chunked-prefill + decode") + " query tok/s",
+            "workload": ("8 x 512-token prefill chunks on cached context U[0,2048]" +
+                         ("" if prefill_only else " + 56 decode rows with context U[256,4096]") +
+                         ", 16q/2kv, d128, one ragged launch per step"),
             "value": h.sum_over_ranks(T) / step_s, "unit": "tok/s", "n_gpus": world,
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms / args.steps,
-            "tokens_per_gpu_step": T, "prefill_tflops_per_step": flops / 1e12,
-            "prefill_tflops_achieved": flops / step_s / 1e12,
-            "tensor_frac_of_peak": flops / step_s / 1e12 / tflops_peak,
-            "decode_bytes_per_step": dbytes, "peak_kind": kind, "dtype": "bf16",
-            "data": "synthetic", "scaling": "weak"}
+            "ms_per_step_per_rank": per_rank, "tokens_per_gpu_step": T,
+            "roofline": {"bound": "tensor", "achieved": achieved, "peak": tflops_peak,
+                         "unit": "TFLOP/s", "frac": achieved / tflops_peak,
+                         "flops_per_step": flops,
+                         "note": "prefill-row FLOPs (4 H D x causal keys) over the whole step "
+                                 "(append, decode rows, tiles, merge)"},
+            "decode_bytes_per_step": dbytes, "peak_kind": f"{kind} bf16 dense (burst)",
+            "gpu_launches": per_step * args.steps, "clocks": clk,
+            "l2": f"{R} rotating batches (> L2 in total)",
+            "dtype": "bf16", "data": "synthetic", "scaling": "weak"}
+
+
+def run_prefill_only(args, rank, world, dist, h):
+    return run_mixed(args, rank, world, dist, h, prefill_only=True)
 
 
 def rope_tables(head_dim, max_len, theta, dev):
@@ -546,13 +808,13 @@ def run_rope(args, rank, world, dist, h):
     for f in fns:
         f()
     torch.cuda.synchronize()
-    ms, _ = h.run_steps(fns, args.steps, args.warmup)
+    ms, _, _ = h.run_steps(fns, args.steps, args.warmup)
     ms = h.max_over_ranks(ms)
     ufns = [unfused(i) for i in range(R)]
     for f in ufns:
         f()
     torch.cuda.synchronize()
-    ums, _ = h.run_steps(ufns, args.steps, args.warmup)
+    ums, _, _ = h.run_steps(ufns, args.steps, args.warmup)
     ums = h.max_over_ranks(ums)
     us, uus = ms * 1e3 / args.steps, ums * 1e3 / args.steps
     nbytes = T * (2 * HEADS + 4 * KV_HEADS) * HEAD_DIM * 2 + T * 2 * HEAD_DIM * 4 + T * 16
@@ -606,28 +868,34 @@ def run_metadata(args, rank, world, dist, h):
 
     import torch
 
-    from shardserve_b200 import Blocks, DeviceMetadata
+    from shardserve_b200 import DeviceMetadata
 
     rnd = random.Random(args.seed + rank)
     context = 4096
 
+    class Pages:  # the allocator state the metadata build reads: block lists and the count
+        def __init__(self, count):
+            self.count, self.tables = count, {}
+            self.free = list(range(count))
+            rnd.shuffle(self.free)
+
     def plan(specs, blocks):
-        rows, offset, caps = [], 0, {}
+        rows, offset = [], 0
         for i, (cursor, n) in enumerate(specs):
             key = f"r{i}"
-            caps[key] = min(cursor + n + 16, context)
+            cap = min(cursor + n + 16, context)
+            blocks.tables[key] = [blocks.free.pop() for _ in range((cap + 15) // 16)]
             rows.append(dict(request_id=key, tokens=[rnd.randint(1, 150000) for _ in range(n)],
                              context=cursor, positions=list(range(cursor, cursor + n)),
                              offset=offset, query_length=n, sample=True))
             offset += n
-        blocks.reserve(caps)
         return {"rows": rows}
 
     out = {}
     for name, specs in (("decode64", [(rnd.randint(127, 4094), 1) for _ in range(BATCH)]),
                         ("mixed", [(rnd.randint(255, 4094), 1) for _ in range(56)]
                          + [(rnd.randint(0, 2048), 512) for _ in range(8)])):
-        blocks = Blocks(40000)
+        blocks = Pages(40000)
         p = plan(specs, blocks)
         dm = DeviceMetadata(blocks, h.dev, context)
         res = {}
@@ -763,23 +1031,31 @@ def run_layers36(args, rank, world, dist, h):
             sb.ragged_attention_direct(qrot, b.k_pool[l], b.v_pool[l], b.block_tables,
                                        b.seq_ids, b.positions, SCALE)
 
-    step()
+    per_step = launches_per_call(step)
     torch.cuda.synchronize()
-    k = max(1, args.steps // layers)
-    w = max(1, args.warmup // layers)
+    k = max(3, args.steps // layers)
+    w = max(3, args.warmup // layers)
     h.S = min(h.S, 4)
-    ms, _ = h.run_steps([step], k, w)
-    ms = h.max_over_ranks(ms)
+    ms, per_rank, clk = _timed_with_clocks(args, h, [step], k, w)
     step_s = ms / 1e3 / k
     abytes = attention_bytes(mine, HEADS, KV_HEADS, HEAD_DIM) * layers
     peak, _, kind = peaks()
-    achieved = h.sum_over_ranks(abytes) / world / step_s / 1e9
-    return {"metric": "36-layer decode-step RoPE+append+attention tok/s", "workload": "layers36",
+    # Per GPU: its own bytes over the slowest rank's step time (all ranks finish the step).
+    achieved = abytes / step_s / 1e9
+    del b, qs, ks, vs
+    return {"metric": "36-layer decode-step RoPE+append+attention tok/s", "workload":
+            "256 sequences (split over the GPUs), context U[512,8192], 16q/2kv, d128, 36 "
+            "per-layer pools; per layer fused RoPE (theta 1e6) + append, then attention",
             "value": h.sum_over_ranks(T) / step_s, "unit": "tok/s", "n_gpus": world,
-            "steps": k, "warmup": w, "ms_per_step": ms / k, "tokens_per_gpu_step": T,
-            "bytes_per_gpu_step": abytes, "hbm_gbs_per_gpu": achieved,
-            "hbm_frac": achieved / peak, "peak_kind": kind, "dtype": "bf16",
-            "data": "synthetic (random-init projections)", "scaling": "strong"}
+            "steps": k, "warmup": w, "ms_per_step": ms / k, "ms_per_step_per_rank": per_rank,
+            "tokens_per_gpu_step": T, "bytes_per_gpu_step": abytes,
+            "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
+                         "frac": achieved / peak,
+                         "note": "attention algorithmic bytes of the 36 layers over the whole "
+                                 "step (36 RoPE+append and 36 attention calls)"},
+            "peak_kind": f"{kind} copy bandwidth", "gpu_launches": per_step * k, "clocks": clk,
+            "l2": "~1.1 GB of K/V per layer per GPU read every step (> L2)",
+            "dtype": "bf16", "data": "synthetic (random-init projections)", "scaling": "strong"}
 
 
 def run_tp2long(args, rank, world, dist, h):
@@ -807,23 +1083,34 @@ def run_tp2long(args, rank, world, dist, h):
         sb.ragged_attention_direct(b.q, b.k_pool, b.v_pool, b.block_tables, b.seq_ids,
                                    b.positions, SCALE)
 
-    step()
+    per_step = launches_per_call(step)
     torch.cuda.synchronize()
-    ms, _ = h.run_steps([step], args.steps, args.warmup)
-    ms = h.max_over_ranks(ms)
+    ms, per_rank, clk = _timed_with_clocks(args, h, [step], args.steps, args.warmup)
     step_s = ms / 1e3 / args.steps
     abytes = attention_bytes(mine, 8, 1, HEAD_DIM)
     peak, _, kind = peaks()
     achieved = abytes / step_s / 1e9
+    pool_gb = 2 * b.k_pool.numel() * 2 / 1e9
+    del b
     # A decode token of a TP2 pair is complete when both ranks did their halves.
     seqs_all = 32 if world >= 2 else T
-    return {"metric": "TP2 long-context decode tok/s", "workload": "tp2long",
+    return {"metric": "TP2 long-context decode tok/s", "workload":
+            "TP2 per-rank heads (8 q / 1 kv, d128), 32 sequences per TP2 pair (split over "
+            "pairs), context U[16384,32768], pool ~60 % of HBM with scattered pages",
+            "layout": (f"{max(1, world // 2)} TP2 pair(s), both ranks of a pair compute their "
+                       "head half of the pair's sequences" if world >= 2 else
+                       "one rank's half (8 q / 1 kv heads) of all 32 sequences"),
             "value": seqs_all / step_s, "unit": "tok/s", "n_gpus": world, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": ms / args.steps,
-            "seqs_per_rank": T, "pool_gb": 2 * b.k_pool.numel() * 2 / 1e9,
-            "bytes_per_rank_step": abytes, "hbm_gbs_per_rank": achieved,
-            "hbm_frac": achieved / peak, "peak_kind": kind, "dtype": "bf16",
-            "data": "synthetic", "scaling": "strong"}
+            "ms_per_step_per_rank": per_rank, "seqs_per_rank": T, "pool_gb": pool_gb,
+            "bytes_per_rank_step": abytes,
+            "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
+                         "frac": achieved / peak,
+                         "note": "one rank's attention algorithmic bytes over the step "
+                                 "(append + attention)"},
+            "peak_kind": f"{kind} copy bandwidth", "gpu_launches": per_step * args.steps,
+            "clocks": clk, "l2": "~400 MB of K/V read per step (> L2)",
+            "dtype": "bf16", "data": "synthetic", "scaling": "strong"}
 
 
 def run_e2e(args, b, dev, h, tokens_all):
@@ -922,7 +1209,8 @@ def traffic_from_profile():
         return None
 
 
-RUNNERS = {"decode64": run_decode64, "mixed": run_mixed, "layers36": run_layers36,
+RUNNERS = {"decode64": run_decode64, "mixed": run_mixed, "prefill_only": run_prefill_only,
+           "layers36": run_layers36,
            "tp2long": run_tp2long, "rope": run_rope, "metadata": run_metadata,
            "tp2oproj": run_tp2oproj}
 

@@ -224,9 +224,11 @@ SS_API int ss_ragged_paged_attention(const void* q, const int64_t q_strides[3], 
  * rejected with SS_ERR_WORKSPACE and a message; use ss_ragged_paged_attention instead.
  * The first call on a device looks up the array's device address (cudaGetSymbolAddress) and
  * the kernels' launch attributes; make that first call before any stream capture.  All
- * calls on a device share the one array and each call overwrites it (its error word is
- * cleared at the start of every call), so calls that can overlap on the GPU (different
- * streams, or concurrent graph replays) race and must be serialised by the caller.
+ * calls on a device share the one array and each call overwrites its scratch part, so
+ * calls that can overlap on the GPU (different streams, or concurrent graph replays) race
+ * and must be serialised by the caller.  The array's error word (SS_DEVERR_* bits) starts
+ * at zero when the library loads and collects the bits of every call on the device until
+ * ss_noalloc_fetch_device_errors reads and clears it.
  * Arguments and results are those of ss_ragged_paged_attention.
  */
 SS_API int ss_ragged_paged_attention_noalloc(
@@ -244,12 +246,28 @@ SS_API int ss_ragged_paged_attention_noalloc(
 SS_API int ss_fetch_device_errors(void* workspace, int clear, uint32_t* flags, void* stream);
 
 /*
+ * The error word of ss_ragged_paged_attention_noalloc's fixed scratch on `device`: reads the
+ * SS_DEVERR_* bits its calls on that device have collected and, if clear != 0, zeroes them.
+ * No counterpart in the reference (it completes the allocation-free entry point, whose
+ * callers have no workspace pointer to pass to ss_fetch_device_errors).  Synchronises
+ * `stream` (a stream of `device`); for tests and debugging, not for the hot path.
+ */
+SS_API int ss_noalloc_fetch_device_errors(int device, int clear, uint32_t* flags, void* stream);
+
+/*
  * Which kernel family the last successful ss_ragged_paged_attention call on this thread
  * used: 1 = TMA/tensor-core split-K kernel, 2 = generic strided kernel (layouts the TMA
  * path cannot describe), 3 = split-K kernel for isolated tokens plus tcgen05 tiles for the
  * chunked-prefill runs, 0 = none yet.  Lets tests assert the fast path really ran.
  */
 SS_API int ss_last_attention_path(void);
+
+/*
+ * Kernels this library has enqueued since it was loaded (every entry point, all threads;
+ * a launch recorded into a CUDA graph counts once, when it is recorded).  Lets a benchmark
+ * state how many of its own kernels one step runs.  No counterpart in the reference.
+ */
+SS_API unsigned long long ss_kernel_launch_count(void);
 
 #ifdef __cplusplus
 }

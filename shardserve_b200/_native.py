@@ -71,7 +71,10 @@ SIGNATURES = {
         ctypes.c_int, ctypes.c_int, ctypes.c_int, ctypes.c_int64, ctypes.c_float, _vp]),
     "ss_fetch_device_errors": (ctypes.c_int, [
         _vp, ctypes.c_int, ctypes.POINTER(ctypes.c_uint32), _vp]),
+    "ss_noalloc_fetch_device_errors": (ctypes.c_int, [
+        ctypes.c_int, ctypes.c_int, ctypes.POINTER(ctypes.c_uint32), _vp]),
     "ss_last_attention_path": (ctypes.c_int, []),
+    "ss_kernel_launch_count": (ctypes.c_ulonglong, []),
 }
 
 

@@ -1,10 +1,12 @@
-"""Paged KV pool for B200, a drop-in for shardserve/cache.py's `Blocks` and `Cache`.
+"""Paged KV pool for B200, a drop-in for shardserve/cache.py's `Cache`.
 
-`Blocks` is the host-side logical page allocator (all-or-nothing reservations, reference
-cache.py:6-35); `Cache` owns the device pools `k`, `v` of shape
+`Cache` owns the device pools `k`, `v` of shape
 [layers, blocks + 8, 16, kv_heads / world, head_dim] (cache.py:37-45; the last eight pages
 are graph-padding scratch, runtime.py:41-44) and appends through the sm_100a kernel
-(`Cache.write`, cache.py:47-49).
+(`Cache.write`, cache.py:47-49).  The logical page allocator `Cache.blocks` (free list and
+per-request block tables, cache.py:6-35) is host-side engine code, not part of the device
+path: it is the engine's own class, by default the reference's `shardserve.cache.Blocks`,
+or any class passed as `allocator`.
 
 Layout in HBM: one contiguous bf16 tensor per K and per V; page p of layer l for KV head h
 is the 16 x head_dim block at [l, p, :, h, :], so one page of all KV heads of a layer is a
@@ -13,55 +15,30 @@ attention kernel moves with a single TMA box.
 """
 from __future__ import annotations
 
-import math
-
 from .kernel import KernelUnsupported, kv_append, rope_kv_append
 
 
-class Blocks:
-    """Free-list page allocator with all-or-nothing reservations (reference cache.py:6-35)."""
-
-    def __init__(self, count):
-        if type(count) is not int or count < 1:
-            raise ValueError("positive block count required")
-        self.count = count
-        self.free = list(range(count))
-        self.tables = {}
-
-    def reserve(self, requests):
-        """Reserves ceil(n / 16) pages for every request of {key: tokens}, or none at all."""
-        if any(key in self.tables for key in requests):
-            raise ValueError("duplicate reservation")
-        if any(type(n) is not int or n < 1 for n in requests.values()):
-            raise ValueError("invalid reservation")
-        sizes = {key: math.ceil(n / 16) for key, n in requests.items()}
-        if sum(sizes.values()) > len(self.free):
-            raise MemoryError("KV capacity exhausted")
-        for key, n in sizes.items():
-            # Pages come off the end of the free list, as in the reference (cache.py:23).
-            self.tables[key] = [self.free.pop() for _ in range(n)]
-        self.check()
-
-    def release(self, key):
-        if key not in self.tables:
-            raise ValueError("double/foreign release")
-        self.free.extend(self.tables.pop(key))
-        self.check()
-
-    def check(self):
-        owned = [b for table in self.tables.values() for b in table]
-        assert sorted(owned + self.free) == list(range(self.count)), "leak/duplicate ownership"
+def default_allocator():
+    """The engine's logical page allocator class: shardserve.cache.Blocks (cache.py:6-35)."""
+    try:
+        from shardserve.cache import Blocks
+    except ImportError as e:
+        raise ImportError(
+            "Cache needs the engine's logical page allocator: pass allocator=<class taking the "
+            "block count> or make the shardserve package importable") from e
+    return Blocks
 
 
 class Cache:
-    """Device KV pool with the reference constructor signature (cache.py:37-45)."""
+    """Device KV pool with the reference constructor signature (cache.py:37-45).  `allocator`
+    builds `self.blocks` from the block count (default: the reference's Blocks)."""
 
-    def __init__(self, c, world, blocks, device, dtype):
+    def __init__(self, c, world, blocks, device, dtype, allocator=None):
         import torch
 
         if torch.device(device).type != "cuda" or dtype != torch.bfloat16:
             raise KernelUnsupported("the B200 KV pool is a BF16 CUDA tensor")
-        self.blocks = Blocks(blocks)
+        self.blocks = (allocator or default_allocator())(blocks)
         self.shape = (c["num_hidden_layers"], blocks + 8, 16, c["num_key_value_heads"] // world,
                       c["hidden_size"] // c["num_attention_heads"])
         self.k = torch.zeros(self.shape, device=device, dtype=dtype)

@@ -5,6 +5,7 @@
 #include <cuda.h>
 #include <cuda_runtime.h>
 
+#include <atomic>
 #include <cmath>
 #include <cstdarg>
 #include <cstdio>
@@ -18,6 +19,9 @@ namespace {
 
 thread_local std::string g_message;
 thread_local int g_last_path = 0;
+// Kernels this library has enqueued (launched, or recorded into a stream capture).
+std::atomic<unsigned long long> g_launches{0};
+void count_launch(unsigned n = 1) { g_launches.fetch_add(n, std::memory_order_relaxed); }
 
 int fail(int status, const char* fmt, ...) {
   char buf[512];
@@ -142,6 +146,10 @@ const char* ss_last_error_message(void) { return g_message.c_str(); }
 
 int ss_last_attention_path(void) { return g_last_path; }
 
+unsigned long long ss_kernel_launch_count(void) {
+  return g_launches.load(std::memory_order_relaxed);
+}
+
 int ss_kv_append(const void* k, const int64_t k_strides[3], const void* v,
                  const int64_t v_strides[3], void* k_pool, const int64_t k_pool_strides[4],
                  void* v_pool, const int64_t v_pool_strides[4], const void* slots,
@@ -185,6 +193,7 @@ int ss_kv_append(const void* k, const int64_t k_strides[3], const void* v,
                    vec_ok(k_pool, k_pool_strides, 4) && vec_ok(v_pool, v_pool_strides, 4);
   const cudaError_t e = ss::launch_kv_append(a, vec, static_cast<cudaStream_t>(stream));
   if (e != cudaSuccess) return cuda_fail(e, "kv_append launch");
+  count_launch();
   return SS_OK;
 }
 
@@ -256,6 +265,7 @@ int ss_rope_kv_append(const void* q, const int64_t q_strides[3], void* q_out,
                    vec_ok(sin_table, sin_strides, 2, 4);
   const cudaError_t e = ss::launch_rope_append(r, vec, static_cast<cudaStream_t>(stream));
   if (e != cudaSuccess) return cuda_fail(e, "rope_kv_append launch");
+  count_launch();
   return SS_OK;
 }
 
@@ -294,6 +304,7 @@ int ss_build_metadata(const int64_t* packed, int64_t rows, int64_t n_selected, i
   m.err = workspace ? static_cast<unsigned*>(workspace) : nullptr;
   const cudaError_t e = ss::launch_build_metadata(m, static_cast<cudaStream_t>(stream));
   if (e != cudaSuccess) return cuda_fail(e, "build_metadata launch");
+  count_launch();
   return SS_OK;
 }
 
@@ -411,6 +422,7 @@ int ss_tp2_oproj_allreduce(const void* attn, const int64_t attn_strides[2], cons
   o.err = static_cast<unsigned*>(workspace);
   const cudaError_t e = ss::launch_tp2_oproj(tmA, tmW, o, static_cast<cudaStream_t>(stream));
   if (e != cudaSuccess) return cuda_fail(e, "tp2_oproj launch");
+  count_launch();
   return SS_OK;
 }
 
@@ -523,12 +535,15 @@ int ss_ragged_paged_attention(const void* q, const int64_t q_strides[3], const v
       d.desc = reinterpret_cast<int4*>(ws + ss::kWsHeader + g.part_bytes);
       e = ss::launch_decode(g, tmK, tmV, d, s);
       if (e != cudaSuccess) return cuda_fail(e, "decode attention launch");
+      count_launch();
       if (prefill) {
         e = ss::launch_prefill(tmQ, tmKp, tmVp, a, s);
         if (e != cudaSuccess) return cuda_fail(e, "prefill attention launch");
+        count_launch();
       }
       e = ss::launch_merge(g, d, s);
       if (e != cudaSuccess) return cuda_fail(e, "split-K merge launch");
+      count_launch();
       g_last_path = prefill ? 3 : 1;
       return SS_OK;
     }
@@ -536,6 +551,7 @@ int ss_ragged_paged_attention(const void* q, const int64_t q_strides[3], const v
   // ---- generic strided path -------------------------------------------------------------
   e = ss::launch_generic_attention(a, s);
   if (e != cudaSuccess) return cuda_fail(e, "generic attention launch");
+  count_launch();
   g_last_path = 2;
   return SS_OK;
 }

@@ -10,7 +10,10 @@
 // How: the split-K scratch lives in a fixed-size array in this library's own device memory
 // (file-scope __device__ storage), and the call passes that array as the workspace of the
 // ordinary entry point.  The array exists on every GPU that loads this library, from load
-// until process exit, whether or not this entry point is used.
+// until process exit, whether or not this entry point is used.  It is zero when the library
+// loads; every call leaves the chunked-prefill work counter in it at zero, and the error
+// word at its start collects SS_DEVERR_* bits across calls until
+// ss_noalloc_fetch_device_errors reads and clears it.
 #include <cuda_runtime.h>
 
 #include <mutex>
@@ -29,33 +32,37 @@ constexpr int kMaxDevices = 64;
 std::mutex g_mu;
 void* g_scratch_addr[kMaxDevices] = {};
 
-// Device address of g_scratch on the current device, looked up once per device.  The host
-// symbol g_scratch is only a stand-in for the device array and must never be handed to a
-// kernel; cudaGetSymbolAddress gives the real device address.
-int scratch_address(void** out, int* device) {
-  cudaError_t e = cudaGetDevice(device);
-  if (e != cudaSuccess) {
-    ss::set_error_message("cudaGetDevice failed: %s", cudaGetErrorString(e));
-    return SS_ERR_CUDA;
-  }
-  if (*device < 0 || *device >= kMaxDevices) {
+// Device address of g_scratch on `device`, which must be the current device, looked up once
+// per device.  The host symbol g_scratch is only a stand-in for the device array and must
+// never be handed to a kernel; cudaGetSymbolAddress gives the real device address.
+int scratch_address_on(int device, void** out) {
+  if (device < 0 || device >= kMaxDevices) {
     ss::set_error_message("device %d is beyond the %d devices the no-allocation path supports",
-                          *device, kMaxDevices);
+                          device, kMaxDevices);
     return SS_ERR_UNSUPPORTED;
   }
   std::lock_guard<std::mutex> lock(g_mu);
-  if (!g_scratch_addr[*device]) {
+  if (!g_scratch_addr[device]) {
     void* p = nullptr;
-    e = cudaGetSymbolAddress(&p, g_scratch);
+    const cudaError_t e = cudaGetSymbolAddress(&p, g_scratch);
     if (e != cudaSuccess || !p) {
       ss::set_error_message("cudaGetSymbolAddress of the static scratch failed: %s",
                             cudaGetErrorString(e));
       return SS_ERR_CUDA;
     }
-    g_scratch_addr[*device] = p;
+    g_scratch_addr[device] = p;
   }
-  *out = g_scratch_addr[*device];
+  *out = g_scratch_addr[device];
   return SS_OK;
+}
+
+int scratch_address(void** out, int* device) {
+  const cudaError_t e = cudaGetDevice(device);
+  if (e != cudaSuccess) {
+    ss::set_error_message("cudaGetDevice failed: %s", cudaGetErrorString(e));
+    return SS_ERR_CUDA;
+  }
+  return scratch_address_on(*device, out);
 }
 
 }  // namespace
@@ -88,15 +95,32 @@ extern "C" int ss_ragged_paged_attention_noalloc(
         need, kScratchBytes);
     return SS_ERR_WORKSPACE;
   }
-  // The error word at the start of the scratch must start at zero for this call.
-  cudaError_t e = cudaMemsetAsync(scratch, 0, sizeof(uint32_t), static_cast<cudaStream_t>(stream));
-  if (e != cudaSuccess) {
-    ss::set_error_message("clearing the scratch error word failed: %s", cudaGetErrorString(e));
-    return SS_ERR_CUDA;
-  }
   return ss_ragged_paged_attention(q, q_strides, k_pool, k_pool_strides, v_pool, v_pool_strides,
                                    block_tables, bt_strides, bt_rows, bt_cols, bt_is_int64,
                                    query_seq_ids, seq_ids_is_int64, positions, positions_is_int64,
                                    out, out_strides, tokens, heads, kv_heads, head_dim, num_pages,
                                    sm_scale, scratch, kScratchBytes, stream);
+}
+
+extern "C" int ss_noalloc_fetch_device_errors(int device, int clear, uint32_t* flags,
+                                              void* stream) {
+  if (!flags) {
+    ss::set_error_message("null pointer argument");
+    return SS_ERR_INVALID;
+  }
+  int prev = 0;
+  cudaError_t e = cudaGetDevice(&prev);
+  if (e != cudaSuccess) {
+    ss::set_error_message("cudaGetDevice failed: %s", cudaGetErrorString(e));
+    return SS_ERR_CUDA;
+  }
+  if (device != prev && (e = cudaSetDevice(device)) != cudaSuccess) {
+    ss::set_error_message("cudaSetDevice(%d) failed: %s", device, cudaGetErrorString(e));
+    return SS_ERR_CUDA;
+  }
+  void* scratch = nullptr;
+  int rc = scratch_address_on(device, &scratch);
+  if (rc == SS_OK) rc = ss_fetch_device_errors(scratch, clear, flags, stream);
+  if (device != prev) cudaSetDevice(prev);
+  return rc;
 }

@@ -12,7 +12,10 @@
 //
 // The per-device workspace (error word, split-K partial states, split descriptors) is kept
 // here: one zero-filled byte buffer per device, grown (never during CUDA graph capture) to
-// what ss_attention_workspace_bytes asks for.
+// what ss_attention_workspace_bytes asks for.  A buffer that is replaced by a larger one is
+// never freed: CUDA graphs captured while it was current keep its address in their kernel
+// arguments and write into it on every replay (decode-bucket graphs captured at start-up,
+// then a larger eager chunked-prefill step, as the reference engine runs).
 #include <torch/extension.h>
 
 #include <ATen/cuda/CUDAContext.h>
@@ -24,6 +27,7 @@
 #include <mutex>
 #include <string>
 #include <tuple>
+#include <vector>
 
 #include "shardserve_b200.h"
 
@@ -104,6 +108,10 @@ void* stream_of(const at::Device& d) {
 std::mutex g_ws_mu;
 // Leaked on purpose: tensors must not be released after the CUDA context is torn down.
 auto* g_ws = new std::map<int, at::Tensor>();
+// Workspaces replaced by a larger one, kept alive for the life of the process: a graph
+// captured earlier still replays into them.  Growth doubles the size, so what is kept here
+// stays below the size of the current workspace.
+auto* g_ws_retired = new std::vector<at::Tensor>();
 auto* g_ws_need = new std::map<std::tuple<int, int64_t, int, int, int>, size_t>();
 
 at::Tensor ensure_workspace(const at::Device& dev, int64_t tokens, int heads, int kv_heads,
@@ -133,6 +141,7 @@ at::Tensor ensure_workspace(const at::Device& dev, int64_t tokens, int heads, in
   const int64_t old = it != g_ws->end() ? it->second.numel() : 0;
   const int64_t size = std::max<int64_t>({static_cast<int64_t>(need), 2 * old, int64_t{1} << 20});
   at::Tensor ws = at::zeros({size}, at::TensorOptions().dtype(at::kByte).device(dev));
+  if (it != g_ws->end()) g_ws_retired->push_back(it->second);
   (*g_ws)[idx] = ws;
   return ws;
 }

@@ -127,6 +127,18 @@ def uniform_lengths(n, lo, hi, seed):
     return torch.randint(lo, hi + 1, (n,), generator=g).tolist()
 
 
+def mixed_rows(seed, chunks=8, decode_rows=56, chunk=512):
+    """The mixed chunked-prefill batch: `decode_rows` decode rows with context U[256, 4096]
+    first (as the reference scheduler packs decode rows first, scheduler.py:119-131), then
+    `chunks` prefill chunks of `chunk` query tokens on cached context U[0, 2048]."""
+    import torch
+
+    g = torch.Generator().manual_seed(seed)
+    decode = [(int(c) - 1, 1) for c in torch.randint(256, 4097, (decode_rows,), generator=g)]
+    prefill = [(int(c), chunk) for c in torch.randint(0, 2049, (chunks,), generator=g)]
+    return decode, prefill
+
+
 def attention_bytes(lengths, heads, kv_heads, head_dim, tokens=None) -> int:
     """Algorithmic HBM bytes of one decode attention launch, each byte counted once:
     K and V of every attended key (GQA re-reads not credited), q in, out, the block-table

@@ -1,7 +1,7 @@
 """Generates tests/golden/<case>.npz by running the REFERENCE implementation itself.
 
 For every case of cases.py this script imports ShardServe unchanged from the reference
-checkout (default /root/reference, override with SHARDSERVE_REFERENCE) and records:
+checkout (the directory named by the SHARDSERVE_REFERENCE environment variable) and records:
 
 * kpool_sha256 / vpool_sha256 — the bf16 pools after the reference's Cache.write
   (shardserve/cache.py:47-49, torch index_copy_), for the bit-exact append check;
@@ -29,7 +29,9 @@ HERE = os.path.dirname(os.path.abspath(__file__))
 sys.path.insert(0, HERE)
 import cases  # noqa: E402
 
-REF = os.environ.get("SHARDSERVE_REFERENCE", "/root/reference")
+REF = os.environ.get("SHARDSERVE_REFERENCE")
+if not REF:
+    sys.exit("set SHARDSERVE_REFERENCE to the reference checkout (its shardserve package)")
 sys.path.insert(0, REF)
 from shardserve import kernel as ref_kernel  # noqa: E402
 from shardserve.cache import Cache as RefCache  # noqa: E402

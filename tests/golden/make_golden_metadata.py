@@ -1,7 +1,7 @@
 """Generates tests/golden/metadata_<case>.npz by running the REFERENCE metadata build itself.
 
 For every plan below this script imports ShardServe unchanged from the reference checkout
-(default /root/reference, override with SHARDSERVE_REFERENCE), reserves the plan's requests
+(the directory named by the SHARDSERVE_REFERENCE environment variable), reserves the plan's requests
 in the reference's own `Blocks` allocator (shardserve/cache.py:6-35, so block ids follow its
 free-list order) and records the output of `metadata(plan, cache, 'cpu', context, bucket)`
 (shardserve/runtime.py:28-49).  Stored: the plan (as JSON text), the block tables, the
@@ -20,7 +20,9 @@ import sys
 import numpy as np
 
 HERE = os.path.dirname(os.path.abspath(__file__))
-REF = os.environ.get("SHARDSERVE_REFERENCE", "/root/reference")
+REF = os.environ.get("SHARDSERVE_REFERENCE")
+if not REF:
+    sys.exit("set SHARDSERVE_REFERENCE to the reference checkout (its shardserve package)")
 sys.path.insert(0, REF)
 from shardserve.cache import Blocks  # noqa: E402
 from shardserve.runtime import metadata  # noqa: E402

@@ -1,7 +1,7 @@
 """Generates tests/golden/rope_<case>.npz by running the REFERENCE RoPE + append itself.
 
 For every case below this script imports ShardServe unchanged from the reference checkout
-(default /root/reference, override with SHARDSERVE_REFERENCE), builds the fp32 cos / sin
+(the directory named by the SHARDSERVE_REFERENCE environment variable), builds the fp32 cos / sin
 tables with the reference's `build_rope_cache` (shardserve/math.py:12-20), rotates seeded
 bf16 q / k with the reference's `apply_rope` (math.py:28-38, torch CPU, bf16 tensors), and
 appends the rotated k and the raw v with the reference's `Cache.write` (cache.py:47-49).
@@ -24,7 +24,9 @@ import numpy as np
 import torch
 
 HERE = os.path.dirname(os.path.abspath(__file__))
-REF = os.environ.get("SHARDSERVE_REFERENCE", "/root/reference")
+REF = os.environ.get("SHARDSERVE_REFERENCE")
+if not REF:
+    sys.exit("set SHARDSERVE_REFERENCE to the reference checkout (its shardserve package)")
 sys.path.insert(0, REF)
 from shardserve.cache import Cache as RefCache  # noqa: E402
 from shardserve.math import apply_rope, build_rope_cache  # noqa: E402

@@ -3,12 +3,55 @@ from __future__ import annotations
 
 import json
 import os
+import sys
 
 import numpy as np
 
 import cases
 
 GOLDEN = os.path.join(os.path.dirname(os.path.abspath(__file__)), "golden")
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+
+
+def reference_blocks():
+    """The reference's own logical page allocator class (shardserve/cache.py:6-35), from its
+    offline install next to the repository (baseline/_ref) or the checkout named by
+    SHARDSERVE_REFERENCE; None where neither is present."""
+    for path in (os.environ.get("SHARDSERVE_REFERENCE"), os.path.join(ROOT, "baseline", "_ref")):
+        if path and os.path.isdir(os.path.join(path, "shardserve")) and path not in sys.path:
+            sys.path.append(path)
+    try:
+        from shardserve.cache import Blocks
+    except ImportError:
+        return None
+    return Blocks
+
+
+class FreeListPages:
+    """Test stand-in for the engine's page allocator where the reference is not installed:
+    the attributes the device path's callers read (tables, count) and all-or-nothing
+    reservations popping pages off the end of a free list, as the reference allocator does
+    (shardserve/cache.py:14-30)."""
+
+    def __init__(self, count):
+        self.count = count
+        self.free = list(range(count))
+        self.tables = {}
+
+    def reserve(self, requests):
+        sizes = {key: (n + 15) // 16 for key, n in requests.items()}
+        if sum(sizes.values()) > len(self.free):
+            raise MemoryError("KV capacity exhausted")
+        for key, n in sizes.items():
+            self.tables[key] = [self.free.pop() for _ in range(n)]
+
+    def release(self, key):
+        self.free.extend(self.tables.pop(key))
+
+
+def page_allocator():
+    """The reference's allocator class where available, else the test stand-in."""
+    return reference_blocks() or FreeListPages
 
 # Parity bar for attention outputs (bf16 result vs fp32 reference), from the task contract.
 MAX_ABS_TOL = 2e-2

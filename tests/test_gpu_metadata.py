@@ -9,7 +9,8 @@ import pytest
 import torch
 
 from oracle.metadata import metadata as oracle_metadata
-from shardserve_b200 import Blocks, DeviceMetadata
+from helpers import page_allocator
+from shardserve_b200 import DeviceMetadata
 from shardserve_b200 import kernel as K
 from shardserve_b200.metadata import metadata as device_metadata
 
@@ -70,7 +71,7 @@ def test_device_metadata_tracks_admissions_and_releases(dev):
     """Steps with new requests, released and re-reserved keys, padding buckets and the
     drop-in function; every step equals the oracle on the allocator's current tables."""
     rnd = random.Random(7)
-    blocks = Blocks(6000)
+    blocks = page_allocator()(6000)
     cache = type("C", (), {})()
     cache.blocks = blocks
     dm = DeviceMetadata(blocks, dev, 4096, capacity=24)

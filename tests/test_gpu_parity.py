@@ -12,7 +12,7 @@ import cases
 import oracle
 import shardserve_b200 as sb
 from helpers import (MAX_ABS_TOL, MEAN_ABS_TOL, bf16_tensor, bits_of, load_golden,
-                     oracle_inputs)
+                     oracle_inputs, page_allocator)
 from shardserve_b200 import kernel as K
 
 pytestmark = pytest.mark.gpu
@@ -196,6 +196,44 @@ def test_cuda_graph_capture_and_replay(dev):
     assert torch.equal(out, want)
 
 
+def test_workspace_growth_keeps_a_captured_graphs_buffer_alive(dev):
+    """A decode graph is captured, then a larger call grows the per-device workspace (as an
+    eager chunked-prefill step after start-up bucket capture does).  The graph still
+    replays into the old buffer, so that buffer must stay allocated: a tensor allocated
+    after the growth must not receive the graph's writes, and the replay stays correct."""
+    from shardserve_b200 import _native
+
+    inp = cases.build("graph_padding")
+    eager = run(inp, to_device(inp, dev))
+    static = to_device(inp, dev)
+    kp0, vp0 = static["kp"].clone(), static["vp"].clone()
+    s = torch.cuda.Stream()
+    s.wait_stream(torch.cuda.current_stream())
+    with torch.cuda.stream(s):
+        for _ in range(3):
+            run(inp, static)
+    torch.cuda.current_stream().wait_stream(s)
+    static["kp"].copy_(kp0)
+    static["vp"].copy_(vp0)
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g):
+        out = run(inp, static)
+    torch.cuda.synchronize()
+    old = K.workspace_for(dev)
+    old_ptr, old_n = old.data_ptr(), old.numel()
+    del old
+    # Enough tokens that the split descriptors alone outgrow the current buffer.
+    _native.ops().ensure_workspace(dev.index, old_n // 16 + 1, 16, 2, 128)
+    assert K.workspace_for(dev).data_ptr() != old_ptr
+    canary = torch.full((old_n,), 0x5A, dtype=torch.uint8, device=dev)
+    static["kp"].copy_(kp0)
+    static["vp"].copy_(vp0)
+    g.replay()
+    torch.cuda.synchronize()
+    assert torch.equal(out, eager)
+    assert bool((canary == 0x5A).all()), "a graph replay wrote into memory it no longer owns"
+
+
 def test_out_of_range_metadata_is_flagged_not_faulted(dev):
     inp = cases.build("config1_decode")
     t = to_device(inp, dev)
@@ -286,7 +324,7 @@ def test_full_size_properties(dev):
 
 def test_cache_object_matches_reference_layout(dev):
     c = dict(num_hidden_layers=3, num_key_value_heads=2, hidden_size=2048, num_attention_heads=16)
-    cache = sb.Cache(c, 1, 64, dev, torch.bfloat16)
+    cache = sb.Cache(c, 1, 64, dev, torch.bfloat16, allocator=page_allocator())
     assert cache.shape == (3, 72, 16, 2, 128)
     inp = cases.build("config1_decode")
     t = to_device(inp, dev)

@@ -1,11 +1,15 @@
 """GPU test of ss_ragged_paged_attention_noalloc, the allocation-free entry point.
 
 Callers that cannot allocate device memory around an attention call (code recorded into a
-CUDA graph, serving loops with a fixed memory plan, FFI hosts without a caching allocator)
-use this entry point; it keeps its split-K scratch in the library's own fixed device array.
-The test drives it through the C ABI directly and checks, on two different calls in a row,
-that its output matches the ordinary entry point (which takes a caller workspace) within
-the attention tolerance used throughout the tests.  The file name makes pytest collect it
+CUDA graph, where cudaMalloc is not allowed; serving loops with a fixed memory plan, where
+an allocation can stall the device; FFI hosts without a caching allocator to keep a
+workspace alive) use this entry point: it keeps its split-K scratch in the library's own
+fixed device array.  The test drives it through the C ABI directly, on two different calls
+in a row, and checks that its output is bit-identical to the ordinary entry point (which
+takes a caller workspace and runs the same kernels on the same inputs) and within the
+attention tolerance of the CPU oracle; that the fast kernels ran; that the error word of
+the fixed scratch reports an out-of-range page through ss_noalloc_fetch_device_errors; and
+that calls beyond the fixed scratch are rejected.  The file name makes pytest collect it
 last.
 """
 import ctypes
@@ -15,9 +19,11 @@ import pytest
 import torch
 
 import cases
+import oracle
 import shardserve_b200 as sb
-from helpers import MAX_ABS_TOL, MEAN_ABS_TOL, bf16_tensor
+from helpers import MAX_ABS_TOL, MEAN_ABS_TOL, bf16_tensor, oracle_inputs
 from shardserve_b200 import _native
+from shardserve_b200 import kernel as K
 
 pytestmark = pytest.mark.gpu
 
@@ -35,8 +41,9 @@ def _device_inputs(name, dev):
     return inp, t
 
 
-def _noalloc(t, scale):
-    q, kp, vp, bt = t["q"], t["kp"], t["vp"], t["bt"]
+def _noalloc(t, scale, bt=None):
+    q, kp, vp = t["q"], t["kp"], t["vp"]
+    bt = t["bt"] if bt is None else bt
     out = torch.empty_like(q)
     s = _native.strides
     rc = _native.lib().ss_ragged_paged_attention_noalloc(
@@ -49,18 +56,51 @@ def _noalloc(t, scale):
     return out
 
 
+def _noalloc_errors(dev, clear=True):
+    flags = ctypes.c_uint32(0)
+    rc = _native.lib().ss_noalloc_fetch_device_errors(
+        dev.index, int(clear), ctypes.byref(flags), torch.cuda.current_stream(dev).cuda_stream)
+    assert rc == _native.SS_OK, _native.last_error()
+    return flags.value
+
+
 def test_noalloc_matches_workspace_entry_point_on_consecutive_calls():
     assert torch.cuda.is_available()
     dev = torch.device("cuda", 0)
+    # The first call on a device resolves the scratch address; it must come before any
+    # stream capture, which this test does not do.
     for name in ("long_decode", "chunked_mixed"):  # two calls in a row, different shapes
         inp, t = _device_inputs(name, dev)
         want = sb.ragged_attention_direct(t["q"], t["kp"], t["vp"], t["bt"], t["seq"],
                                           t["pos"], inp["scale"])
+        path = K.last_attention_path()
         got = _noalloc(t, inp["scale"])
         torch.cuda.synchronize()
-        err = (got.float() - want.float()).abs()
-        assert err.max().item() <= MAX_ABS_TOL
-        assert err.mean().item() <= MEAN_ABS_TOL
+        assert _native.lib().ss_last_attention_path() == path
+        assert path in (1, 3), "the TMA / tensor-core kernels did not run"
+        # Same kernels, same inputs, same launch shapes: the same bits.
+        assert torch.equal(got, want)
+        q, kp, vp = oracle_inputs(inp)
+        ref = oracle.ragged_attention(q, kp, vp, inp["block_tables"], inp["seq_ids"],
+                                      inp["positions"], inp["scale"])
+        err = np.abs(got.float().cpu().numpy() - ref)
+        assert err.max() <= MAX_ABS_TOL, err.max()
+        assert err.mean() <= MEAN_ABS_TOL, err.mean()
+    assert _noalloc_errors(dev) == 0
+
+
+def test_noalloc_error_word_reports_a_page_outside_the_pool():
+    assert torch.cuda.is_available()
+    dev = torch.device("cuda", 0)
+    inp, t = _device_inputs("config1_decode", dev)
+    _noalloc(t, inp["scale"])
+    _noalloc_errors(dev, clear=True)
+    bt = t["bt"].clone()
+    bt[0, 0] = t["kp"].shape[0] + 1000  # outside the pool: the page reads as zeros
+    _noalloc(t, inp["scale"], bt=bt)
+    _noalloc(t, inp["scale"])  # a clean call after it keeps the bit
+    assert _noalloc_errors(dev, clear=True) & _native.SS_DEVERR_PAGE
+    assert _noalloc_errors(dev) == 0
 
 
 def test_noalloc_rejects_calls_beyond_its_fixed_scratch():
