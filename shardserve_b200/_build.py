@@ -6,7 +6,9 @@ statically, so the single .so is all a GPU host needs next to this package.
 """
 from __future__ import annotations
 
+import concurrent.futures
 import os
+import shlex
 import shutil
 import subprocess
 import sys
@@ -49,22 +51,29 @@ def up_to_date() -> bool:
 
 
 def build(force: bool = False, verbose: bool = False, ptxas_info: bool = False) -> str:
-    """Compiles every .cu source into LIB_PATH; returns the library path."""
+    """Compiles every .cu source (in parallel) into LIB_PATH; returns the library path.
+    Extra nvcc flags (for example -D overrides of tuning constants) come from the
+    SS_NVCC_FLAGS environment variable."""
     if not force and not ptxas_info and up_to_date():
         return LIB_PATH
     nvcc = _nvcc()
-    objs = []
     tmp_dir = os.path.join(PKG_DIR, "_build")
     os.makedirs(tmp_dir, exist_ok=True)
+    extra = shlex.split(os.environ.get("SS_NVCC_FLAGS", ""))
+    cmds = []
     for src in SOURCES:
         obj = os.path.join(tmp_dir, src.replace(".cu", ".o"))
-        cmd = [nvcc, *NVCC_FLAGS, "-c", os.path.join(CSRC, src), "-o", obj]
+        cmd = [nvcc, *NVCC_FLAGS, *extra, "-c", os.path.join(CSRC, src), "-o", obj]
         if ptxas_info:
             cmd.insert(1, "-Xptxas=-v")
         if verbose:
             print(" ".join(cmd), file=sys.stderr)
-        subprocess.run(cmd, check=True)
-        objs.append(obj)
+        cmds.append((cmd, obj))
+    workers = max(1, min(len(cmds), os.cpu_count() or 1))
+    with concurrent.futures.ThreadPoolExecutor(max_workers=workers) as ex:
+        for f in [ex.submit(subprocess.run, cmd, check=True) for cmd, _ in cmds]:
+            f.result()
+    objs = [obj for _, obj in cmds]
     tmp_lib = LIB_PATH + ".tmp"
     cmd = [nvcc, "-gencode", "arch=compute_100a,code=sm_100a", "-shared", "-o", tmp_lib, *objs,
            "-Xcompiler", "-fPIC"]

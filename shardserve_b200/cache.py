@@ -31,16 +31,22 @@ def default_allocator():
 
 class Cache:
     """Device KV pool with the reference constructor signature (cache.py:37-45).  `allocator`
-    builds `self.blocks` from the block count (default: the reference's Blocks)."""
+    builds `self.blocks` from the block count (default: the reference's Blocks).
+    `scratch_pages` trailing pages serve graph-padding rows, one page per padding row (the
+    reference keeps 8 for its buckets of up to 8 rows; DecodeGraphs buckets of up to n rows
+    need n)."""
 
-    def __init__(self, c, world, blocks, device, dtype, allocator=None):
+    def __init__(self, c, world, blocks, device, dtype, allocator=None, scratch_pages=8):
         import torch
 
         if torch.device(device).type != "cuda" or dtype != torch.bfloat16:
             raise KernelUnsupported("the B200 KV pool is a BF16 CUDA tensor")
+        if scratch_pages < 0:
+            raise KernelUnsupported("scratch_pages must be >= 0")
         self.blocks = (allocator or default_allocator())(blocks)
-        self.shape = (c["num_hidden_layers"], blocks + 8, 16, c["num_key_value_heads"] // world,
-                      c["hidden_size"] // c["num_attention_heads"])
+        self.scratch_pages = int(scratch_pages)
+        self.shape = (c["num_hidden_layers"], blocks + self.scratch_pages, 16,
+                      c["num_key_value_heads"] // world, c["hidden_size"] // c["num_attention_heads"])
         self.k = torch.zeros(self.shape, device=device, dtype=dtype)
         self.v = torch.zeros_like(self.k)
         self.bytes = 2 * self.k.numel() * self.k.element_size()

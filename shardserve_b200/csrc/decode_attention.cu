@@ -41,6 +41,49 @@ namespace ss {
 namespace {
 
 constexpr int kMinChunk = 4;  // pages: lower bound on a CTA's share (limits tiny splits)
+// Pages of its first row a CTA prefetches into L2 before it waits for the preceding grid
+// (its block-table entries are read before that wait): the prefetches stream while the
+// preceding kernels finish, and the first TMA loads after the wait hit L2.  Measured on the
+// batch-64 workload (graph-replayed steps): 0 pages 32.9 us, 4 pages 30.5 us, 8 pages 31.4.
+#ifndef SS_DECODE_L2_PREFETCH_PAGES
+#define SS_DECODE_L2_PREFETCH_PAGES 4
+#endif
+constexpr int kPrefetchPages = SS_DECODE_L2_PREFETCH_PAGES;
+#ifndef SS_PDL_DECODE_EARLY
+#define SS_PDL_DECODE_EARLY 1
+#endif
+// When the split-K merge lets the next grid on the stream launch: 1 at its entry, 2 once the
+// decode grid before it is complete (after its griddepcontrol.wait), 0 never (at its end).
+// With 1, the next call's CTAs launch during this call's decode and hold SM slots that this
+// call's late decode CTAs need (long-context TP2 step: 81.5 us against 75.0 with 2); with 2
+// the next call's prologue still overlaps the merge and the append (batch-64 decode step:
+// 31.6 us, against 33.8 with 0).
+#ifndef SS_PDL_MERGE_EARLY
+#define SS_PDL_MERGE_EARLY 2
+#endif
+// Decode-only shape with two KV heads per CTA: depth of each CTA's stage ring, and the CTAs
+// per SM its launch bounds assume (its register cap); shared memory sets the actual count.
+#ifndef SS_DECODE_NARROW_STAGES
+#define SS_DECODE_NARROW_STAGES 3
+#endif
+#ifndef SS_DECODE_NARROW_REG_CTAS
+#define SS_DECODE_NARROW_REG_CTAS 3
+#endif
+// Merge kernel: parts of a split row whose (m, l) it stages in shared memory per round, parts
+// folded from registers in one round trip, and CTAs per SM its launch bounds assume.
+#ifndef SS_MERGE_BATCH
+#define SS_MERGE_BATCH 64
+#endif
+#ifndef SS_MERGE_DIRECT
+#define SS_MERGE_DIRECT 16
+#endif
+#ifndef SS_MERGE_MIN_CTAS
+#define SS_MERGE_MIN_CTAS 1
+#endif
+// Merge grid: CTAs per SM (at most; fewer when there are fewer work items).
+#ifndef SS_MERGE_GRID_PER_SM
+#define SS_MERGE_GRID_PER_SM 8
+#endif
 // Consumer warps per KV head of the wide configuration.  A warp holds its stage while it
 // computes the page, so the ring keeps (stages - warps per head) pages in flight: 5 warps
 // with 9 stages measured best (6 with 8: a decode-heavy mixed step 146.9 us against 140.0;
@@ -90,9 +133,10 @@ template <int HD, int KVB, int NG, int PR>
 struct Traits {
   static constexpr int kNCW = PR * KVB;  // consumer warps: (KV head, page parity)
   static constexpr int kThreads = 32 * (kNCW + 1);
-  static constexpr int kMinBlocks = PR > 2 ? 1 : (KVB == 2 ? 3 : 4);  // CTAs per SM
+  // CTAs per SM the register cap assumes (shared memory sets the resident count).
+  static constexpr int kRegBlocks = PR > 2 ? 1 : (KVB == 2 ? SS_DECODE_NARROW_REG_CTAS : 4);
   static constexpr int kSlab = kPage * KVB * HD * 2;   // one page of K (or V), KVB heads
-  static constexpr int kStages = PR > 2 ? (KVB == 2 ? 9 : 18) : (KVB == 2 ? 3 : 5);
+  static constexpr int kStages = PR > 2 ? (KVB == 2 ? 9 : 18) : (KVB == 2 ? SS_DECODE_NARROW_STAGES : 5);
   static constexpr int kStageBytes = 2 * kSlab;
   static constexpr int kRows = 16 * KVB;  // query-head rows per partial slot
   static constexpr int kSlotFloats = kRows * (HD + 2);
@@ -213,7 +257,7 @@ __device__ __forceinline__ uint32_t slab_addr(uint32_t slab, int g, int kk, int 
 }
 
 template <int HD, int KVB, int NG, int PR>
-__global__ void __launch_bounds__(Traits<HD, KVB, NG, PR>::kThreads, Traits<HD, KVB, NG, PR>::kMinBlocks)
+__global__ void __launch_bounds__(Traits<HD, KVB, NG, PR>::kThreads, Traits<HD, KVB, NG, PR>::kRegBlocks)
     decode_attention_kernel(const __grid_constant__ CUtensorMap tmK,
                             const __grid_constant__ CUtensorMap tmV, const DecodeArgs d) {
   using Tr = Traits<HD, KVB, NG, PR>;
@@ -248,6 +292,12 @@ __global__ void __launch_bounds__(Traits<HD, KVB, NG, PR>::kThreads, Traits<HD, 
     // start at once (on the SMs this grid leaves free) instead of after the prologue.
     griddep_wait();
     griddep_launch_dependents();
+  } else {
+#if SS_PDL_DECODE_EARLY
+    // Decode-only launches: the next grid on the stream (the split-K merge) may start at
+    // once; it waits for this grid before it reads anything this grid writes.
+    griddep_launch_dependents();
+#endif
   }
 
   // ---- prologue: total units, this CTA's range, and its first (row, page) ------------
@@ -258,6 +308,9 @@ __global__ void __launch_bounds__(Traits<HD, KVB, NG, PR>::kThreads, Traits<HD, 
   auto note_empty = [&](long long t, long long u) {
     // t < 2^31 (token indices are int in the stage metadata): a 32-bit modulo
     if (static_cast<unsigned>(t) % static_cast<unsigned>(d.G) != blockIdx.x) return;
+    // The preceding grids (the append, and before it the previous call's merge, which
+    // reads the descriptors) may still run: wait for them before writing.
+    griddep_wait();
     for (int b = 0; b < d.nkvblk; ++b) d.desc[t * d.nkvblk + b] = make_int4(0, 0, 0, 0);
     if (u < 0) write_zero_token(a, t);
   };
@@ -436,13 +489,26 @@ __global__ void __launch_bounds__(Traits<HD, KVB, NG, PR>::kThreads, Traits<HD, 
     // Block-table entries of the first 32 pages do not depend on the preceding kernel:
     // fetch them before waiting for it.
     int pf_page = -1;
+    // The first row's token data, also taken before the wait and reused for its segment
+    // (after griddepcontrol.wait these loads would miss L1 again).
+    int np_first = 0;
+    TokInfo ti_first;
     {
       const long long t = r / d.nkvblk;
+      token_units(d, t, false, &np_first);
       const TokInfo ti = token_info(a, t, false);
+      ti_first = ti;
       const int idx = p + lane;
       if (idx < min(ti.npages, p + remaining)) {
         const long long pid = ld_index(a.bt, a.bt64, ti.seq * a.bt_sb + idx * a.bt_sn);
         pf_page = (pid < 0 || pid >= a.N) ? -2 : static_cast<int>(pid);
+      }
+      // Pool pages are written only by the preceding append, through L2, so a prefetch
+      // issued before waiting for it never leaves a stale copy behind.
+      if (lane < kPrefetchPages && pf_page >= 0) {
+        const int b0 = static_cast<int>(r % d.nkvblk);
+        tma_prefetch_5d(&tmK, 0, 0, 0, b0 * KVB, pf_page);
+        tma_prefetch_5d(&tmV, 0, 0, 0, b0 * KVB, pf_page);
       }
     }
     bool use_pf = true;
@@ -458,13 +524,19 @@ __global__ void __launch_bounds__(Traits<HD, KVB, NG, PR>::kThreads, Traits<HD, 
         break;
       }
       int np = 0;
-      token_units(d, t, false, &np);
+      TokInfo ti;
+      if (use_pf) {  // the first row: its data came before the wait
+        np = np_first;
+        ti = ti_first;
+      } else {
+        token_units(d, t, false, &np);
+        ti = token_info(a, t, false);
+      }
       if (p >= np) {
         ++r;
         p = 0;
         continue;
       }
-      const TokInfo ti = token_info(a, t, false);
       const int seg_end = min(np, p + remaining);
       const bool whole = (p == 0 && seg_end == np);
       const long long row_start = u - p;
@@ -479,17 +551,10 @@ __global__ void __launch_bounds__(Traits<HD, KVB, NG, PR>::kThreads, Traits<HD, 
       }
       if (p == 0 && lane == 0)  // this CTA holds the row's first page: describe the split
         d.desc[r] = make_int4(whole ? 1 : nparts, cfirst, late, 0);
-      int next_row = -1;  // the next row with pages inside this CTA's range, if any
-      if (remaining > seg_end - p) {
-        for (long long r2 = r + 1; r2 < a.T * d.nkvblk; ++r2) {
-          int np2 = 0;
-          token_units(d, r2 / d.nkvblk, false, &np2);
-          if (np2 > 0) {
-            next_row = static_cast<int>(r2);
-            break;
-          }
-        }
-      }
+      // The next row with pages inside this CTA's range, if any (lets consumers prefetch
+      // its queries); looked up after the segment's first copies are issued.
+      int next_row = -1;
+      bool next_known = remaining <= seg_end - p;
       const long long bt_row = ti.seq * a.bt_sb;
       for (int pb = p; pb < seg_end && ok; pb += 32) {
         const int idx = pb + lane;
@@ -515,6 +580,24 @@ __global__ void __launch_bounds__(Traits<HD, KVB, NG, PR>::kThreads, Traits<HD, 
             if (!mbar_wait(bar_empty + 8 * stage, phase ^ 1)) {
               ok = false;
             } else {
+              // Copies first (expected bytes without the arrival), then the stage metadata,
+              // then the arrival that lets the consumers read both.
+              const uint32_t dst = sbase + stage * Tr::kStageBytes;
+              mbar_expect_tx(bar_full + 8 * stage, Tr::kStageBytes);
+              tma_load_5d(dst, &tmK, bar_full + 8 * stage, 0, 0, 0, b * KVB, pg, policy);
+              tma_load_5d(dst + Tr::kSlab, &tmV, bar_full + 8 * stage, 0, 0, 0, b * KVB, pg,
+                          policy);
+              if (!next_known) {
+                for (long long r2 = r + 1; r2 < a.T * d.nkvblk; ++r2) {
+                  int np2 = 0;
+                  token_units(d, r2 / d.nkvblk, false, &np2);
+                  if (np2 > 0) {
+                    next_row = static_cast<int>(r2);
+                    break;
+                  }
+                }
+                next_known = true;
+              }
               StageMeta m;
               m.t = static_cast<int>(t);
               m.b = b;
@@ -527,11 +610,7 @@ __global__ void __launch_bounds__(Traits<HD, KVB, NG, PR>::kThreads, Traits<HD, 
               m.cfirst = cfirst;
               m.next_row = next_row;
               meta[stage] = m;
-              const uint32_t dst = sbase + stage * Tr::kStageBytes;
-              mbar_arrive_expect_tx(bar_full + 8 * stage, Tr::kStageBytes);
-              tma_load_5d(dst, &tmK, bar_full + 8 * stage, 0, 0, 0, b * KVB, pg, policy);
-              tma_load_5d(dst + Tr::kSlab, &tmV, bar_full + 8 * stage, 0, 0, 0, b * KVB, pg,
-                          policy);
+              mbar_arrive(bar_full + 8 * stage);
             }
           }
           ok = __shfl_sync(0xffffffffu, ok, 0);
@@ -890,13 +969,13 @@ __global__ void __launch_bounds__(Traits<HD, KVB, NG, PR>::kThreads, Traits<HD, 
 // over many SMs.  Items are compacted per CTA first, so rows that were not split (or that
 // belong to another kernel) cost one descriptor read.
 template <int HD, int KVB>
-__global__ void __launch_bounds__(16 * KVB * 8) merge_partials_kernel(const DecodeArgs d) {
+__global__ void __launch_bounds__(16 * KVB * 8, SS_MERGE_MIN_CTAS) merge_partials_kernel(const DecodeArgs d) {
   constexpr int R = 16 * KVB;      // query-head rows per partial slot
   constexpr int NT = R * 8;        // (row, float4 of a 32-dim slice) per thread
   constexpr int NSL = HD / 32;     // slices per row
   constexpr int SF = R * (HD + 2);  // floats per partial slot
-  constexpr int kDirect = 16;      // parts folded from registers in one round trip
-  constexpr int kBatch = 64;       // parts per shared-memory batch beyond that
+  constexpr int kDirect = SS_MERGE_DIRECT;  // parts folded from registers in one round trip
+  constexpr int kBatch = SS_MERGE_BATCH;  // parts per shared-memory batch beyond that
   __shared__ float Mp[kBatch][R];
   __shared__ float Lp[kBatch][R];
   __shared__ long long items[NT];
@@ -906,7 +985,15 @@ __global__ void __launch_bounds__(16 * KVB * 8) merge_partials_kernel(const Deco
   const int tid = threadIdx.x, row = tid >> 3, f = tid & 7;
   const int group = a.group;
   const bool valid = (row & 15) < group;
+#if SS_PDL_MERGE_EARLY == 1
+  // The next grid on the stream may start at once (a following append or attention call
+  // waits for this grid before it touches memory this grid reads or writes).
+  griddep_launch_dependents();
+#endif
   griddep_wait();  // every partial and descriptor of the decode grid is visible
+#if SS_PDL_MERGE_EARLY == 2
+  griddep_launch_dependents();
+#endif
   const long long nitems = a.T * d.nkvblk * NSL;
   const long long stride = static_cast<long long>(gridDim.x) * NT;
   for (long long base = blockIdx.x; base < nitems; base += stride) {
@@ -1109,7 +1196,7 @@ bool geometry_for(int device, long long tokens, int kv_heads, DecodeGeometry* g,
   g->smem = Tr::kSmemBytes;
   g->part_bytes = partial_region_bytes(device, why);
   g->desc_bytes = align_up(static_cast<size_t>(tokens) * g->nkvblk * sizeof(int4), 256);
-  g->merge_grid = sms * 8;
+  g->merge_grid = sms * SS_MERGE_GRID_PER_SM;
   return true;
 }
 

@@ -3,13 +3,21 @@
 //
 // Slot s addresses row s % 16 of page s / 16.  One thread moves one 16-byte vector (8 bf16)
 // when both sides are 16-byte addressable along head_dim, else one element.  The copy is
-// bit-exact.  The kernel releases its dependent grid at once (programmatic dependent
-// launch) so the attention kernel that follows can run its prologue while the append
-// drains; the attention kernel waits (griddepcontrol.wait) before it reads any page.
+// bit-exact.
+//
+// Programmatic dependent launch on both sides: the kernel is launched so that it may start
+// while the preceding kernel on the stream finishes (it then waits, griddepcontrol.wait,
+// before it reads k / v or writes the pool), and it releases its dependent grid at entry,
+// so the attention kernel that follows runs its prologue while the append drains; the
+// attention kernel waits for the append before it reads any page.
 #include <cuda_bf16.h>
 
 #include "attention.cuh"
 #include "ptx.cuh"
+
+#ifndef SS_PDL_APPEND
+#define SS_PDL_APPEND 1
+#endif
 
 namespace ss {
 
@@ -18,6 +26,7 @@ namespace {
 template <bool VEC>
 __global__ void __launch_bounds__(256) kv_append_kernel(const AppendArgs a) {
   griddep_launch_dependents();
+  griddep_wait();  // k / v may come from the preceding kernel, which may still read the pool
   constexpr int E = VEC ? 8 : 1;  // elements per thread
   const long long per_row = static_cast<long long>(a.KVH) * a.D / E;
   const long long total = a.T * per_row;
@@ -61,11 +70,17 @@ cudaError_t launch_kv_append(const AppendArgs& a, bool vectorised, cudaStream_t 
   long long blocks = (work + 255) / 256;
   if (blocks > 148 * 32) blocks = 148 * 32;
   if (blocks < 1) blocks = 1;
-  if (vectorised)
-    kv_append_kernel<true><<<static_cast<unsigned>(blocks), 256, 0, stream>>>(a);
-  else
-    kv_append_kernel<false><<<static_cast<unsigned>(blocks), 256, 0, stream>>>(a);
-  return cudaGetLastError();
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(static_cast<unsigned>(blocks));
+  cfg.blockDim = dim3(256);
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = SS_PDL_APPEND ? 1 : 0;
+  return vectorised ? cudaLaunchKernelEx(&cfg, kv_append_kernel<true>, a)
+                    : cudaLaunchKernelEx(&cfg, kv_append_kernel<false>, a);
 }
 
 }  // namespace ss

@@ -37,7 +37,10 @@ __device__ __forceinline__ float bf16r(float x) {
 
 template <bool VEC>
 __global__ void __launch_bounds__(256) rope_append_kernel(const RopeArgs r) {
+  // Programmatic dependent launch both ways (as kv_append_kernel): release the attention
+  // kernel at entry, wait for the preceding kernel before reading q / k / v.
   griddep_launch_dependents();
+  griddep_wait();
   const AppendArgs& a = r.app;
   constexpr int E = VEC ? 8 : 1;  // elements per half (rotation) or per copy (v)
   const int half = a.D / 2;
@@ -152,11 +155,17 @@ cudaError_t launch_rope_append(const RopeArgs& r, bool vectorised, cudaStream_t 
   long long blocks = (r.app.T * per_tok + 255) / 256;
   if (blocks > 148 * 32) blocks = 148 * 32;
   if (blocks < 1) blocks = 1;
-  if (vectorised)
-    rope_append_kernel<true><<<static_cast<unsigned>(blocks), 256, 0, stream>>>(r);
-  else
-    rope_append_kernel<false><<<static_cast<unsigned>(blocks), 256, 0, stream>>>(r);
-  return cudaGetLastError();
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(static_cast<unsigned>(blocks));
+  cfg.blockDim = dim3(256);
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return vectorised ? cudaLaunchKernelEx(&cfg, rope_append_kernel<true>, r)
+                    : cudaLaunchKernelEx(&cfg, rope_append_kernel<false>, r);
 }
 
 }  // namespace ss

@@ -127,8 +127,11 @@ class DeviceMetadata:
                        tables=torch.empty((n, self.width), dtype=torch.int32, device=dev),
                        seqs=torch.empty(tokens, dtype=torch.int32, device=dev),
                        slots=torch.empty(tokens, dtype=torch.long, device=dev),
-                       selected=torch.empty(len(sel), dtype=torch.long, device=dev))
+                       selected=torch.empty(len(sel), dtype=torch.long, device=self.device))
         else:
+            if "selected" not in out:  # a graph's static inputs carry no sampled indices
+                out = dict(out, selected=torch.empty(len(sel), dtype=torch.long,
+                                                     device=self.device))
             self._check_out(out, n, tokens, len(sel))
         ws = workspace_for(self.device)
         rc = _native.lib().ss_build_metadata(

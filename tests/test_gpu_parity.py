@@ -222,8 +222,17 @@ def test_workspace_growth_keeps_a_captured_graphs_buffer_alive(dev):
     old = K.workspace_for(dev)
     old_ptr, old_n = old.data_ptr(), old.numel()
     del old
-    # Enough tokens that the split descriptors alone outgrow the current buffer.
-    _native.ops().ensure_workspace(dev.index, old_n // 16 + 1, 16, 2, 128)
+    # A token count whose workspace need (asked of the library) outgrows the current buffer.
+    import ctypes
+
+    tokens, need = 1024, ctypes.c_size_t(0)
+    while True:
+        assert _native.lib().ss_attention_workspace_bytes(dev.index, tokens, 16, 2, 128,
+                                                          ctypes.byref(need)) == _native.SS_OK
+        if need.value > old_n:
+            break
+        tokens *= 2
+    _native.ops().ensure_workspace(dev.index, tokens, 16, 2, 128)
     assert K.workspace_for(dev).data_ptr() != old_ptr
     canary = torch.full((old_n,), 0x5A, dtype=torch.uint8, device=dev)
     static["kp"].copy_(kp0)
