@@ -145,8 +145,8 @@ SS_API int ss_build_metadata(const int64_t* packed, int64_t rows, int64_t n_sele
  * attn        : bf16 [tokens, in_features] (this rank's heads), unit column stride
  * w_o         : bf16 [out_features, in_features] (this rank's column shard of o_proj)
  * out         : bf16 [tokens, out_features]
- * local_inbox / peer_inbox: 8 * max_tokens * out_features bytes on this rank / the other
- *               rank (its buffer opened with ss_ipc_open), zeroed once
+ * local_inbox / peer_inbox: 6 * ceil(max_tokens / 32) * 32 * out_features bytes on this
+ *               rank / the other rank (its buffer opened with ss_ipc_open), zeroed once
  *               (ss_device_alloc_zeroed) and never cleared again
  * epoch_counter: 8 zeroed device bytes per rank that count its calls (the kernel advances
  *               them, so calls can be replayed from a CUDA graph)

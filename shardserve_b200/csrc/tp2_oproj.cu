@@ -13,12 +13,15 @@
 // 64-column K chunks (128-byte swizzle), so a call with K = 1024 needs 8-16 copies per CTA;
 // warp 1 (one thread) issues tcgen05.mma M128 N(tile) K16 into TMEM.  All four warps then
 // read their 32-token TMEM quadrant 32 features at a time and round P_r to bf16.  The
-// exchange uses flag-carrying words: every 8-byte word holds two bf16 partials and the
-// call's epoch, stored with 16-byte volatile stores straight into the
-// other rank's inbox over NVLink; the other rank polls its own inbox words until their
-// epoch is the current one (bounded), so no fence or separate flag is needed, and adds
-// them to its own partial.  Inbox halves alternate by call parity, so a rank never
-// overwrites words the other rank has not read.  The epoch lives in device memory: every
+// exchange uses flag-carrying vectors: every 16-byte vector holds six bf16 partials (three
+// feature pairs) and the call's epoch, so a token's 32 features take six vectors, 96 bytes
+// for 64 bytes of payload.  A warp stores each of its six vectors for its 32 tokens as one
+// contiguous 512-byte run (vector-major inbox layout) straight into the other rank's inbox
+// over NVLink; the other rank polls its own inbox, with the same coalesced 16-byte loads,
+// until every vector carries the current epoch (bounded), so no fence or separate flag is
+// needed, and adds the pairs to its own partial.  A vector is written and read whole
+// (st / ld .v4.b32 of one aligned 16-byte vector).  Inbox halves alternate by call parity,
+// so a rank never overwrites vectors the other rank has not read.  The epoch lives in device memory: every
 // CTA reads the last completed call number at its start and the last CTA to finish
 // advances it, so calls can be replayed from a CUDA graph.  A CTA waits only for its
 // counterpart on the other GPU, which writes before it waits; the grid is at most one wave,
@@ -37,6 +40,7 @@ constexpr int kTM = 128;    // tokens per tile (MMA M)
 constexpr int kTNMax = 128; // features per tile (MMA N): 32, 64 or 128 by call size
 constexpr int kTK = 64;     // K columns per swizzle atom
 constexpr int kMaxStagesO = 8;
+constexpr int kVecPerGroup = 6;  // inbox vectors per (token, 32 features): 3 bf16 pairs each
 constexpr int kRingBytes = 200 * 1024;
 constexpr int kSmemO = kRingBytes + 512 + 1024;
 
@@ -148,28 +152,37 @@ __global__ void __launch_bounds__(128, 1)
                                                      __uint_as_float(acc[2 * i + 1]));
       pk[i] = *reinterpret_cast<const uint32_t*>(&p);
     }
-    // Inbox word (token, feature pair) = {bf16 pair, epoch}; 16 words per thread and group.
-    const long long word0 = ((static_cast<long long>(epoch & 1u) * o.T_max + row) * o.N + f0) / 2;
+    // Inbox vector v (0..5) of (token row, 32-feature group): {pairs 3v .. 3v + 2, epoch},
+    // laid out [parity][32-row block][feature group][v][row % 32] so that a warp's store of
+    // one vector is 512 contiguous bytes.
+    const long long rb = row >> 5, nfg = o.N / 32;
+    const long long vec0 =
+        (((static_cast<long long>(epoch & 1u) * ((o.T_max + 31) / 32) + rb) * nfg + f0 / 32) *
+         kVecPerGroup) * 32 + (row & 31);
     if (live) {
-      uint2* dst = reinterpret_cast<uint2*>(o.peer_inbox) + word0;
+      uint4* dst = reinterpret_cast<uint4*>(o.peer_inbox) + vec0;
 #pragma unroll
-      for (int q = 0; q < 8; ++q)
-        st_volatile_v4(dst + 2 * q, make_uint4(pk[2 * q], epoch, pk[2 * q + 1], epoch));
+      for (int v = 0; v < kVecPerGroup; ++v) {
+        const uint32_t p0 = pk[3 * v], p1 = 3 * v + 1 < 16 ? pk[3 * v + 1] : 0u;
+        const uint32_t p2 = 3 * v + 2 < 16 ? pk[3 * v + 2] : 0u;
+        st_volatile_v4(dst + 32 * v, make_uint4(p0, p1, p2, epoch));
+      }
     }
-    if (live && !timed_out) {  // the other rank's partial: poll until every word is current
-      const uint2* src = reinterpret_cast<const uint2*>(o.local_inbox) + word0;
-      uint32_t theirs[16];
-      unsigned pending = 0xFFu;  // one bit per 16-byte pair of words
+    if (live && !timed_out) {  // the other rank's partial: poll until every vector is current
+      const uint4* src = reinterpret_cast<const uint4*>(o.local_inbox) + vec0;
+      uint32_t theirs[3 * kVecPerGroup];
+      unsigned pending = (1u << kVecPerGroup) - 1;  // one bit per vector
       const long long start = clock64();
       while (pending) {
 #pragma unroll
-        for (int q = 0; q < 8; ++q) {
-          if (pending & (1u << q)) {
-            const uint4 v = ld_volatile_v4(src + 2 * q);
-            if (v.y == epoch && v.w == epoch) {
-              theirs[2 * q] = v.x;
-              theirs[2 * q + 1] = v.z;
-              pending &= ~(1u << q);
+        for (int v = 0; v < kVecPerGroup; ++v) {
+          if (pending & (1u << v)) {
+            const uint4 x = ld_volatile_v4(src + 32 * v);
+            if (x.w == epoch) {
+              theirs[3 * v] = x.x;
+              theirs[3 * v + 1] = x.y;
+              theirs[3 * v + 2] = x.z;
+              pending &= ~(1u << v);
             }
           }
         }

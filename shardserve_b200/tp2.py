@@ -5,9 +5,10 @@ KV head and the matching column shard of o_proj, and each layer does
 `hidden = hidden + reduce(F.linear(attention, w_o))` with `reduce` = a two-rank NCCL
 all-reduce (shardserve/model.py:40, runtime.py:17-24).  `TP2OprojAllReduce` computes
 `reduce(F.linear(attention, w_o))` in one kernel launch per rank: the GEMM tiles run on the
-tensor cores, each rank stores its bf16 partial of every tile, tagged with the call number,
-straight into the other rank's inbox over NVLink and adds the other rank's partial from its
-own inbox once its tags match, so both ranks return the same bf16 sum.  The inboxes are
+tensor cores, each rank stores its bf16 partial of every tile, six values per 16-byte vector
+tagged with the call number, straight into the other rank's inbox over NVLink and adds the
+other rank's partial from its own inbox once its tags match, so both ranks return the same
+bf16 sum.  The inboxes are
 plain device allocations shared with CUDA IPC once, at construction (a collective over
 `group`).
 """
@@ -37,7 +38,10 @@ class TP2OprojAllReduce:
         lib = _native.lib()
         with torch.cuda.device(self.device):
             self._local = {}
-            for name, nbytes in (("inbox", 8 * self.max_tokens * self.n), ("err", 256),
+            # Two halves (call parity) of [32-row blocks][feature groups][6][32] 16-byte
+            # vectors: 6 * rows rounded up to 32 * out_features bytes.
+            inbox = 6 * ((self.max_tokens + 31) // 32) * 32 * self.n
+            for name, nbytes in (("inbox", inbox), ("err", 256),
                                  ("epoch", 256)):
                 p = ctypes.c_void_p()
                 if lib.ss_device_alloc_zeroed(nbytes, ctypes.byref(p)) != _native.SS_OK:
