@@ -51,6 +51,8 @@ struct DecodeArgs {
   int4* desc;    // [T * nkvblk] split descriptor per row: {parts (0 none, 1 whole), first
                  // CTA, first part in the CTA's second slot, 0}; rewritten every call
   float* part;   // [2 * G] partial-state slots
+  unsigned* gbar;  // grid barrier: arrivals at gbar[0], generation at gbar[32] (workspace
+                   // bytes 72..75 and 200..203)
 };
 
 __device__ __forceinline__ long long ld_index(const void* p, int is64, long long i) {
@@ -116,7 +118,7 @@ __device__ __forceinline__ bool token_in_long_run(const AttnArgs& a, int min_run
 
 // ---- host-side launchers (defined next to their kernels) ------------------------------
 struct DecodeGeometry {
-  int kvb, ng, pr, nkvblk, G, threads, merge_grid;
+  int kvb, ng, pr, nkvblk, G, threads;
   size_t smem;
   size_t desc_bytes, part_bytes;  // workspace regions
 };
@@ -136,8 +138,6 @@ int wide_grid(DecodeGeometry* g, int device, long long rows, long long cols, lon
 // Launches the TMA split-K decode kernel; returns a cudaError_t.
 cudaError_t launch_decode(const DecodeGeometry& g, const CUtensorMap& tmK, const CUtensorMap& tmV,
                           const DecodeArgs& d, cudaStream_t stream);
-// Launches the split-K merge (programmatic dependent launch after the decode kernel).
-cudaError_t launch_merge(const DecodeGeometry& g, const DecodeArgs& d, cudaStream_t stream);
 
 cudaError_t launch_generic_attention(const AttnArgs& a, cudaStream_t stream);
 
@@ -228,9 +228,10 @@ cudaError_t launch_tp2_oproj(const CUtensorMap& tmA, const CUtensorMap& tmW, con
 // Sets the text ss_last_error_message() returns on this thread (printf-style).
 void set_error_message(const char* fmt, ...);
 
-// Workspace layout (fixed per device): [0, 256) header (error word at byte 0), then the
-// partial-state region (sized for the largest decode kernel instance), then one int4 split
-// descriptor per (token, KV block) row.
+// Workspace layout (fixed per device): [0, 256) header (error word at byte 0, chunked-prefill
+// work counter at bytes 64..71, decode grid barrier at bytes 72..75 and 200..203: zero
+// before the first call, left consistent by every call), then the partial-state region (sized for the
+// largest decode kernel instance), then one int4 split descriptor per (token, KV block) row.
 constexpr size_t kWsHeader = 256;
 inline size_t align_up(size_t x, size_t a) { return (x + a - 1) / a * a; }
 

@@ -533,6 +533,7 @@ int ss_ragged_paged_attention(const void* q, const int64_t q_strides[3], const v
       uint8_t* ws = static_cast<uint8_t*>(workspace);
       d.part = reinterpret_cast<float*>(ws + ss::kWsHeader);
       d.desc = reinterpret_cast<int4*>(ws + ss::kWsHeader + g.part_bytes);
+      d.gbar = reinterpret_cast<unsigned*>(ws + 72);
       e = ss::launch_decode(g, tmK, tmV, d, s);
       if (e != cudaSuccess) return cuda_fail(e, "decode attention launch");
       count_launch();
@@ -541,9 +542,6 @@ int ss_ragged_paged_attention(const void* q, const int64_t q_strides[3], const v
         if (e != cudaSuccess) return cuda_fail(e, "prefill attention launch");
         count_launch();
       }
-      e = ss::launch_merge(g, d, s);
-      if (e != cudaSuccess) return cuda_fail(e, "split-K merge launch");
-      count_launch();
       g_last_path = prefill ? 3 : 1;
       return SS_OK;
     }

@@ -17,9 +17,12 @@
 //    base-2 online softmax with quad shuffles, and O^T += V^T.P^T (M = head_dim, N = heads,
 //    K = 16 keys): P goes from the S accumulators straight into the B operand, so the P.V
 //    product wastes no padded rows and the accumulator is head_dim x 8 per warp.
-//  * A token whose pages span several CTAs leaves fp32 partial (m, l, acc) states, which the
-//    split-K merge kernel chained after this one (programmatic dependent launch) folds into
-//    bf16 outputs.  No CTA ever waits for another.
+//  * A token whose pages span several CTAs leaves fp32 partial (m, l, acc) states.  When
+//    every active CTA has streamed its share (a grid-wide barrier: one arrival per CTA, the
+//    last one opens it; all CTAs of the one-wave grid are resident, no grid that could hold
+//    SM slots is released before it, and every wait is bounded), the same CTAs fold those
+//    states into bf16 outputs, each taking (split row, 32-dim slice) items.  Folding inside
+//    the grid saves a second kernel's launch and CTA dispatch on every call.
 //  * Two CTA shapes.  Decode-only launches: two consumer warps per KV head, 3-4 CTAs per SM
 //    on every SM.  Launches followed by chunked-prefill tiles: the wide CTA (five consumer
 //    warps per KV head, a 9-18 stage ring, one CTA per SM) on only as many SMs as the decode
@@ -49,18 +52,6 @@ constexpr int kMinChunk = 4;  // pages: lower bound on a CTA's share (limits tin
 #define SS_DECODE_L2_PREFETCH_PAGES 4
 #endif
 constexpr int kPrefetchPages = SS_DECODE_L2_PREFETCH_PAGES;
-#ifndef SS_PDL_DECODE_EARLY
-#define SS_PDL_DECODE_EARLY 1
-#endif
-// When the split-K merge lets the next grid on the stream launch: 1 at its entry, 2 once the
-// decode grid before it is complete (after its griddepcontrol.wait), 0 never (at its end).
-// With 1, the next call's CTAs launch during this call's decode and hold SM slots that this
-// call's late decode CTAs need (long-context TP2 step: 81.5 us against 75.0 with 2); with 2
-// the next call's prologue still overlaps the merge and the append (batch-64 decode step:
-// 31.6 us, against 33.8 with 0).
-#ifndef SS_PDL_MERGE_EARLY
-#define SS_PDL_MERGE_EARLY 2
-#endif
 // Decode-only shape with two KV heads per CTA: depth of each CTA's stage ring, and the CTAs
 // per SM its launch bounds assume (its register cap); shared memory sets the actual count.
 #ifndef SS_DECODE_NARROW_STAGES
@@ -68,21 +59,6 @@ constexpr int kPrefetchPages = SS_DECODE_L2_PREFETCH_PAGES;
 #endif
 #ifndef SS_DECODE_NARROW_REG_CTAS
 #define SS_DECODE_NARROW_REG_CTAS 3
-#endif
-// Merge kernel: parts of a split row whose (m, l) it stages in shared memory per round, parts
-// folded from registers in one round trip, and CTAs per SM its launch bounds assume.
-#ifndef SS_MERGE_BATCH
-#define SS_MERGE_BATCH 64
-#endif
-#ifndef SS_MERGE_DIRECT
-#define SS_MERGE_DIRECT 16
-#endif
-#ifndef SS_MERGE_MIN_CTAS
-#define SS_MERGE_MIN_CTAS 1
-#endif
-// Merge grid: CTAs per SM (at most; fewer when there are fewer work items).
-#ifndef SS_MERGE_GRID_PER_SM
-#define SS_MERGE_GRID_PER_SM 8
 #endif
 // Consumer warps per KV head of the wide configuration.  A warp holds its stage while it
 // computes the page, so the ring keeps (stages - warps per head) pages in flight: 5 warps
@@ -120,6 +96,7 @@ struct Ctl {
   long long r0;  // first row (token * nkvblk + block)
   int off0;      // first page inside r0
   int found;
+  int merge_mask;  // the grid barrier opened (1) or timed out (0)
   unsigned long long stage_bar;  // mbarrier of the staged index arrays (wide shape)
   long long red[32];
 };
@@ -256,6 +233,147 @@ __device__ __forceinline__ uint32_t slab_addr(uint32_t slab, int g, int kk, int 
   return slab + row * 128 + ((chunk16 ^ (key & 7)) << 4);
 }
 
+// Grid-wide barrier over `n` arrivals, one per CTA.  bar[0] counts this call's arrivals,
+// bar[32] (its own 128-byte line, away from the arrivals) is the generation the waiters
+// poll; both are zero before the first call and the last arrival resets bar[0].  A CTA that
+// has no merge work arrives without waiting (`wait` false).  The arrival is an acq_rel
+// atomic by one thread after a CTA barrier: it releases the CTA's writes (partial states,
+// descriptors) and, for the last arrival, acquires everyone else's; the release store of
+// the new generation hands them on to the waiters.  Returns false if the barrier was not
+// opened within kWaitLimitCycles.
+__device__ bool grid_barrier(unsigned* bar, unsigned n, bool wait) {
+  unsigned* gen_p = bar + 32;
+  const unsigned gen = ld_relaxed_gpu_u32(gen_p);  // read before arriving (ordered by the acq_rel)
+  if (atom_add_acq_rel_gpu_u32(bar, 1u) == n - 1) {
+    st_relaxed_gpu_u32(bar, 0u);
+    st_release_gpu_u32(gen_p, gen + 1u);  // open
+    return true;
+  }
+  if (!wait) return true;
+  const long long start = clock64();
+  while (ld_acquire_gpu_u32(gen_p) == gen) {
+    if (clock64() - start > kWaitLimitCycles) return false;
+    __nanosleep(256);
+  }
+  return true;
+}
+
+// Split-K merge after the grid barrier.  Item = (row, 32-dim slice of head_dim); active CTA
+// c takes items c, c + nactive, ...  A row split over n CTAs left n fp32 partial states
+// (unnormalised O, running max m, running sum l per query head, base 2) in slots 2 (cfirst +
+// p) (+1 for part 0 when the row starts inside CTA cfirst's range).  Per round every thread
+// reads one item's descriptor, the split items are compacted into shared memory, then each
+// thread (valid query-head row, 4 dims) folds up to 8 parts per L2 round trip.  Every read
+// bypasses L1: the parts come from other SMs during this call.
+struct MergeIn {  // what the merge reads and writes (plain values: no kernel-parameter pointer)
+  const int4* desc;
+  const float* part;
+  __nv_bfloat16* out;
+  long long o_st, o_sh, o_sd, T;
+  int nkvblk, group;
+};
+
+template <int HD, int KVB, int NT>
+__device__ __noinline__ void merge_split_rows(const MergeIn d, int cta, int nactive,
+                                              uint8_t* scratch) {
+  constexpr int R = 16 * KVB;       // query-head rows per partial slot
+  constexpr int SF = R * (HD + 2);  // floats per slot
+  constexpr int NSL = HD / 32;      // slices per row
+  constexpr int kDirect = 8;        // parts folded from registers per round trip
+  constexpr int RPP = NT / 8;       // rows per pass (8 threads x 4 dims cover 32 dims)
+  const MergeIn& a = d;
+  const int tid = threadIdx.x;
+  const int group = a.group;
+  const int vrows = KVB * group;    // valid query-head rows of a slot
+  long long* items = reinterpret_cast<long long*>(scratch);
+  int4* descs = reinterpret_cast<int4*>(scratch + NT * sizeof(long long));
+  int* nitems = reinterpret_cast<int*>(scratch + NT * (sizeof(long long) + sizeof(int4)));
+  const long long npairs = a.T * d.nkvblk * NSL;
+  const long long per_round = static_cast<long long>(nactive) * NT;
+  for (long long base = cta; base < npairs; base += per_round) {
+    if (tid == 0) *nitems = 0;
+    named_bar_sync(1, NT);
+    const long long w = base + static_cast<long long>(tid) * nactive;
+    if (w < npairs) {
+      const int4 ds = __ldcg(&d.desc[w / NSL]);
+      if (ds.x >= 2) {
+        const int k = atomicAdd(nitems, 1);
+        items[k] = w;
+        descs[k] = ds;
+      }
+    }
+    named_bar_sync(1, NT);
+    const int n = *nitems;
+    for (int it = 0; it < n; ++it) {
+      const long long rr = items[it] / NSL;
+      const int sl = static_cast<int>(items[it] % NSL);
+      const int4 ds = descs[it];
+      const int nparts = ds.x, cfirst = ds.y, late = ds.z;
+      const long long t = rr / d.nkvblk;
+      const int b = static_cast<int>(rr % d.nkvblk);
+      for (int v0 = 0; v0 < vrows; v0 += RPP) {
+        const int vr = v0 + tid / 8;
+        if (vr >= vrows) continue;
+        const int srow = (vr / group) * 16 + vr % group;
+        const int dcol = sl * 32 + (tid % 8) * 4;
+        float M = -CUDART_INF_F, L = 0.f;
+        float4 o = make_float4(0.f, 0.f, 0.f, 0.f);
+        for (int p0 = 0; p0 < nparts; p0 += kDirect) {
+          float mv[kDirect], lv[kDirect];
+          float4 vv[kDirect];
+#pragma unroll
+          for (int u = 0; u < kDirect; ++u) {
+            mv[u] = -CUDART_INF_F;
+            lv[u] = 0.f;
+            vv[u] = make_float4(0.f, 0.f, 0.f, 0.f);
+            const int pi = p0 + u;
+            if (pi < nparts) {
+              const float* ps =
+                  d.part + static_cast<long long>(2 * (cfirst + pi) + ((pi == 0 && late) ? 1 : 0)) * SF;
+              mv[u] = __ldcg(ps + R * HD + srow);
+              lv[u] = __ldcg(ps + R * HD + R + srow);
+              vv[u] = __ldcg(reinterpret_cast<const float4*>(ps + srow * HD + dcol));
+            }
+          }
+          float Mn = M;
+#pragma unroll
+          for (int u = 0; u < kDirect; ++u) Mn = fmaxf(Mn, mv[u]);
+          const float ms = Mn == -CUDART_INF_F ? 0.f : Mn;
+          const float sc = ex2(M - ms);
+          L *= sc;
+          o.x *= sc;
+          o.y *= sc;
+          o.z *= sc;
+          o.w *= sc;
+#pragma unroll
+          for (int u = 0; u < kDirect; ++u) {
+            const float wgt = ex2(mv[u] - ms);
+            L += lv[u] * wgt;
+            o.x += vv[u].x * wgt;
+            o.y += vv[u].y * wgt;
+            o.z += vv[u].z * wgt;
+            o.w += vv[u].w * wgt;
+          }
+          M = Mn;
+        }
+        const float inv = L > 0.f ? 1.f / L : 0.f;
+        __nv_bfloat16* op = a.out + t * a.o_st +
+                            static_cast<long long>((b * KVB + vr / group) * group + vr % group) * a.o_sh;
+        if (a.o_sd == 1 && (reinterpret_cast<uintptr_t>(op + dcol) & 7) == 0) {
+          *reinterpret_cast<uint2*>(op + dcol) =
+              make_uint2(pack_bf16(o.x * inv, o.y * inv), pack_bf16(o.z * inv, o.w * inv));
+        } else {
+          op[dcol * a.o_sd] = __float2bfloat16(o.x * inv);
+          op[(dcol + 1) * a.o_sd] = __float2bfloat16(o.y * inv);
+          op[(dcol + 2) * a.o_sd] = __float2bfloat16(o.z * inv);
+          op[(dcol + 3) * a.o_sd] = __float2bfloat16(o.w * inv);
+        }
+      }
+    }
+    named_bar_sync(1, NT);  // the compacted list is rebuilt next round
+  }
+}
+
 template <int HD, int KVB, int NG, int PR>
 __global__ void __launch_bounds__(Traits<HD, KVB, NG, PR>::kThreads, Traits<HD, KVB, NG, PR>::kRegBlocks)
     decode_attention_kernel(const __grid_constant__ CUtensorMap tmK,
@@ -292,12 +410,6 @@ __global__ void __launch_bounds__(Traits<HD, KVB, NG, PR>::kThreads, Traits<HD, 
     // start at once (on the SMs this grid leaves free) instead of after the prologue.
     griddep_wait();
     griddep_launch_dependents();
-  } else {
-#if SS_PDL_DECODE_EARLY
-    // Decode-only launches: the next grid on the stream (the split-K merge) may start at
-    // once; it waits for this grid before it reads anything this grid writes.
-    griddep_launch_dependents();
-#endif
   }
 
   // ---- prologue: total units, this CTA's range, and its first (row, page) ------------
@@ -315,6 +427,13 @@ __global__ void __launch_bounds__(Traits<HD, KVB, NG, PR>::kThreads, Traits<HD, 
     if (u < 0) write_zero_token(a, t);
   };
   long long U = 0, chunk = 0, u0 = 0;
+  // A CTA leaving before the streaming phase (no units, or a failed staging copy) still
+  // arrives at the grid barrier, after its descriptor writes, without waiting at it.
+  auto leave_early = [&]() {
+    griddep_wait();
+    __syncthreads();
+    if (tid == 0) grid_barrier(d.gbar, static_cast<unsigned>(d.G), false);
+  };
   // Wide shape: the launch carries thousands of prefill tokens, and a scan that loads them
   // token by token (several dependent round trips per pass, several passes) kept the
   // tiles waiting ~13 us.  Instead the sequence-id and position arrays are copied whole into
@@ -346,7 +465,7 @@ __global__ void __launch_bounds__(Traits<HD, KVB, NG, PR>::kThreads, Traits<HD, 
       if (__syncthreads_or(!mbar_wait(sbar, 0))) {  // CTA-uniform
         if (tid == 0) atomicOr(a.err, SS_DEVERR_TIMEOUT);
         mbar_wait(sbar, 0);  // let the copies land before the CTA releases its memory
-        griddep_wait();
+        leave_early();
         return;
       }
       auto seq_at = [&](long long t) -> long long {
@@ -389,7 +508,7 @@ __global__ void __launch_bounds__(Traits<HD, KVB, NG, PR>::kThreads, Traits<HD, 
       chunk = max((U + ctas - 1) / ctas, static_cast<long long>(kMinChunk));
       u0 = static_cast<long long>(blockIdx.x) * chunk;
       if (u0 >= U) {  // uniform across the CTA; see the wait/trigger order below
-        griddep_wait();
+        leave_early();
         return;
       }
 #pragma unroll 1
@@ -449,7 +568,7 @@ __global__ void __launch_bounds__(Traits<HD, KVB, NG, PR>::kThreads, Traits<HD, 
     chunk = max((U + ctas - 1) / ctas, static_cast<long long>(kMinChunk));
     u0 = static_cast<long long>(blockIdx.x) * chunk;
     if (u0 >= U) {  // uniform across the CTA; see the wait/trigger order below
-      griddep_wait();
+      leave_early();
       return;
     }
 #pragma unroll
@@ -469,7 +588,7 @@ __global__ void __launch_bounds__(Traits<HD, KVB, NG, PR>::kThreads, Traits<HD, 
   }
   __syncthreads();
   if (!ctl->found) {  // cannot happen when u0 < U; uniform across the CTA
-    griddep_wait();
+    leave_early();
     return;
   }
   const int n_units = static_cast<int>(min(chunk, U - u0));
@@ -959,154 +1078,39 @@ __global__ void __launch_bounds__(Traits<HD, KVB, NG, PR>::kThreads, Traits<HD, 
     named_bar_sync(1, Tr::kNCW * 32);  // merge scratch is reused by the next segment
   }
 
+  // ---- grid barrier, then the split-K merge by every active CTA --------------------------
+  // Every CTA of the grid arrives once: the inactive ones (u0 >= U) as they leave the
+  // prologue (after clearing the descriptors of tokens without units here), the active ones
+  // 0 .. nactive - 1 when every consumer warp is done (the CTA's partial states and
+  // descriptors are written: the producer wrote its descriptors before the stage arrivals
+  // the consumers waited for).
+  const int nactive = static_cast<int>((U + chunk - 1) / chunk);
+  named_bar_sync(1, Tr::kNCW * 32);
+  if (tid == 0)
+    ctl->merge_mask = grid_barrier(d.gbar, static_cast<unsigned>(d.G), true) ? 1 : 0;
+  named_bar_sync(1, Tr::kNCW * 32);
+  // Decode-only shape: the next grid on the stream (an append or attention call) may launch
+  // now; its CTAs take SM slots only as this grid's CTAs leave.  (The wide shape released
+  // the prefill tiles at its entry; the grid after them is released by the tiles.)
+  if constexpr (PR <= 2) griddep_launch_dependents();
+  if (!ctl->merge_mask) {
+    if (tid == 0) atomicOr(a.err, SS_DEVERR_TIMEOUT);
+    return;
+  }
+  // The stage ring is idle (every stage was consumed before the kDone stage): merge scratch.
+  MergeIn mi;
+  mi.desc = d.desc;
+  mi.part = d.part;
+  mi.out = a.out;
+  mi.o_st = a.o_st;
+  mi.o_sh = a.o_sh;
+  mi.o_sd = a.o_sd;
+  mi.T = a.T;
+  mi.nkvblk = d.nkvblk;
+  mi.group = a.group;
+  merge_split_rows<HD, KVB, Tr::kNCW * 32>(mi, blockIdx.x, nactive, smem);
 }
 
-// ---- split-K merge -----------------------------------------------------------------------
-// One work item = (split row, 32-dim slice of head_dim); a row split over n CTAs left n fp32
-// partial states (unnormalised O, running max m, running sum l per query head).  The CTA
-// loads every part's (m, l) into shared memory, then each thread (query head, 4 dims) folds
-// all parts with eight float4 loads in flight: a merge costs a few L2 round trips, spread
-// over many SMs.  Items are compacted per CTA first, so rows that were not split (or that
-// belong to another kernel) cost one descriptor read.
-template <int HD, int KVB>
-__global__ void __launch_bounds__(16 * KVB * 8, SS_MERGE_MIN_CTAS) merge_partials_kernel(const DecodeArgs d) {
-  constexpr int R = 16 * KVB;      // query-head rows per partial slot
-  constexpr int NT = R * 8;        // (row, float4 of a 32-dim slice) per thread
-  constexpr int NSL = HD / 32;     // slices per row
-  constexpr int SF = R * (HD + 2);  // floats per partial slot
-  constexpr int kDirect = SS_MERGE_DIRECT;  // parts folded from registers in one round trip
-  constexpr int kBatch = SS_MERGE_BATCH;  // parts per shared-memory batch beyond that
-  __shared__ float Mp[kBatch][R];
-  __shared__ float Lp[kBatch][R];
-  __shared__ long long items[NT];
-  __shared__ int4 descs[NT];
-  __shared__ int nitems_s;
-  const AttnArgs& a = d.a;
-  const int tid = threadIdx.x, row = tid >> 3, f = tid & 7;
-  const int group = a.group;
-  const bool valid = (row & 15) < group;
-#if SS_PDL_MERGE_EARLY == 1
-  // The next grid on the stream may start at once (a following append or attention call
-  // waits for this grid before it touches memory this grid reads or writes).
-  griddep_launch_dependents();
-#endif
-  griddep_wait();  // every partial and descriptor of the decode grid is visible
-#if SS_PDL_MERGE_EARLY == 2
-  griddep_launch_dependents();
-#endif
-  const long long nitems = a.T * d.nkvblk * NSL;
-  const long long stride = static_cast<long long>(gridDim.x) * NT;
-  for (long long base = blockIdx.x; base < nitems; base += stride) {
-    if (tid == 0) nitems_s = 0;
-    __syncthreads();
-    const long long w = base + static_cast<long long>(tid) * gridDim.x;
-    if (w < nitems) {
-      const int4 ds = __ldcg(&d.desc[w / NSL]);
-      if (ds.x >= 2) {
-        const int k = atomicAdd(&nitems_s, 1);
-        items[k] = w;
-        descs[k] = ds;
-      }
-    }
-    __syncthreads();
-    const int n = nitems_s;
-    for (int it = 0; it < n; ++it) {
-      const long long wi = items[it];
-      const long long rr = wi / NSL;
-      const int sl = static_cast<int>(wi % NSL);
-      const int4 ds = descs[it];
-      const int nparts = ds.x, cfirst = ds.y, late = ds.z;
-      auto slot_ptr = [&](int pi) {
-        return d.part + static_cast<long long>(2 * (cfirst + pi) + ((pi == 0 && late) ? 1 : 0)) * SF;
-      };
-      const int dcol = sl * 32 + f * 4;
-      float L = 0.f;
-      float4 o = make_float4(0.f, 0.f, 0.f, 0.f);
-      if (nparts <= kDirect) {
-        // One round trip: every part's (m, l, 4 values) of this thread's head row.
-        float mv[kDirect], lv[kDirect];
-        float4 vv[kDirect];
-#pragma unroll
-        for (int u = 0; u < kDirect; ++u) {
-          mv[u] = -CUDART_INF_F;
-          lv[u] = 0.f;
-          vv[u] = make_float4(0.f, 0.f, 0.f, 0.f);
-          if (u < nparts && valid) {
-            const float* ps = slot_ptr(u);
-            mv[u] = __ldcg(ps + R * HD + row);
-            lv[u] = __ldcg(ps + R * HD + R + row);
-            vv[u] = __ldcg(reinterpret_cast<const float4*>(ps + row * HD + dcol));
-          }
-        }
-        float M = -CUDART_INF_F;
-#pragma unroll
-        for (int u = 0; u < kDirect; ++u) M = fmaxf(M, mv[u]);
-        const float ms = M == -CUDART_INF_F ? 0.f : M;
-#pragma unroll
-        for (int u = 0; u < kDirect; ++u) {
-          const float wgt = ex2(mv[u] - ms);
-          L += lv[u] * wgt;
-          o.x += vv[u].x * wgt;
-          o.y += vv[u].y * wgt;
-          o.z += vv[u].z * wgt;
-          o.w += vv[u].w * wgt;
-        }
-      } else {
-        float M = -CUDART_INF_F;
-        for (int p0 = 0; p0 < nparts; p0 += kBatch) {
-          const int nb = min(kBatch, nparts - p0);
-          __syncthreads();
-          for (int pi = f; pi < nb; pi += 8) {
-            const float* ps = slot_ptr(p0 + pi);
-            Mp[pi][row] = valid ? __ldcg(ps + R * HD + row) : -CUDART_INF_F;
-            Lp[pi][row] = valid ? __ldcg(ps + R * HD + R + row) : 0.f;
-          }
-          __syncthreads();
-          float mb = M;
-          for (int pi = 0; pi < nb; ++pi) mb = fmaxf(mb, Mp[pi][row]);
-          const float ms = mb == -CUDART_INF_F ? 0.f : mb;
-          const float scl = ex2(M - ms);
-          L *= scl;
-          o.x *= scl;
-          o.y *= scl;
-          o.z *= scl;
-          o.w *= scl;
-          M = mb;
-          if (!valid) continue;
-          for (int pi = 0; pi < nb; pi += 8) {
-            float4 v[8];
-#pragma unroll
-            for (int u = 0; u < 8; ++u)
-              if (pi + u < nb)
-                v[u] = __ldcg(reinterpret_cast<const float4*>(slot_ptr(p0 + pi + u) + row * HD + dcol));
-#pragma unroll
-            for (int u = 0; u < 8; ++u)
-              if (pi + u < nb) {
-                const float wgt = ex2(Mp[pi + u][row] - ms);
-                L += Lp[pi + u][row] * wgt;
-                o.x += v[u].x * wgt;
-                o.y += v[u].y * wgt;
-                o.z += v[u].z * wgt;
-                o.w += v[u].w * wgt;
-              }
-          }
-        }
-      }
-      if (valid) {
-        const long long t = rr / d.nkvblk;
-        const int b = static_cast<int>(rr % d.nkvblk);
-        const float inv = L > 0.f ? 1.f / L : 0.f;
-        __nv_bfloat16* op = a.out + t * a.o_st +
-                            static_cast<long long>((b * KVB + (row >> 4)) * group + (row & 15)) * a.o_sh;
-        op[dcol * a.o_sd] = __float2bfloat16(o.x * inv);
-        op[(dcol + 1) * a.o_sd] = __float2bfloat16(o.y * inv);
-        op[(dcol + 2) * a.o_sd] = __float2bfloat16(o.z * inv);
-        op[(dcol + 3) * a.o_sd] = __float2bfloat16(o.w * inv);
-      }
-    }
-    __syncthreads();
-  }
-}
 
 struct CachedOcc {
   int device = -1;
@@ -1196,7 +1200,6 @@ bool geometry_for(int device, long long tokens, int kv_heads, DecodeGeometry* g,
   g->smem = Tr::kSmemBytes;
   g->part_bytes = partial_region_bytes(device, why);
   g->desc_bytes = align_up(static_cast<size_t>(tokens) * g->nkvblk * sizeof(int4), 256);
-  g->merge_grid = sms * SS_MERGE_GRID_PER_SM;
   return true;
 }
 
@@ -1275,24 +1278,6 @@ cudaError_t launch_decode(const DecodeGeometry& g, const CUtensorMap& tmK, const
   SS_LAUNCH(128, 2, 1, kWidePR)
   SS_LAUNCH(128, 1, 1, kWidePR)
 #undef SS_LAUNCH
-  return cudaErrorInvalidValue;
-}
-
-cudaError_t launch_merge(const DecodeGeometry& g, const DecodeArgs& d, cudaStream_t stream) {
-  const long long items = d.a.T * d.nkvblk * (d.a.D / 32);
-  cudaLaunchConfig_t cfg = {};
-  cfg.gridDim = dim3(static_cast<unsigned>(std::min<long long>(items, g.merge_grid)));
-  cfg.blockDim = dim3(16 * g.kvb * 8);
-  cfg.stream = stream;
-  cudaLaunchAttribute attr[1];
-  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
-  attr[0].val.programmaticStreamSerializationAllowed = 1;
-  cfg.attrs = attr;
-  cfg.numAttrs = 1;
-  if (d.a.D == 128 && g.kvb == 2) return cudaLaunchKernelEx(&cfg, merge_partials_kernel<128, 2>, d);
-  if (d.a.D == 128 && g.kvb == 1) return cudaLaunchKernelEx(&cfg, merge_partials_kernel<128, 1>, d);
-  if (d.a.D == 64 && g.kvb == 2) return cudaLaunchKernelEx(&cfg, merge_partials_kernel<64, 2>, d);
-  if (d.a.D == 64 && g.kvb == 1) return cudaLaunchKernelEx(&cfg, merge_partials_kernel<64, 1>, d);
   return cudaErrorInvalidValue;
 }
 
