@@ -585,7 +585,11 @@ def run_decode64(args, rank, world, dist, h):
     batches = [decode_batch(lengths, HEADS, KV_HEADS, HEAD_DIM, seed=args.seed + 1000 * rank + r,
                             device=dev) for r in range(R)]
 
-    def step_fn(b):
+    def step_fn(b):  # Cache.write + ragged_attention_direct, one call (append folded in)
+        return lambda: sb.kv_append_attention(b.k_pool, b.v_pool, b.k_new, b.v_new, b.slots,
+                                              b.q, b.block_tables, b.seq_ids, b.positions, SCALE)
+
+    def two_calls(b):  # the same step as the reference model's two calls (model.py:32-37)
         def f():
             sb.kv_append(b.k_pool, b.v_pool, b.k_new, b.v_new, b.slots)
             sb.ragged_attention_direct(b.q, b.k_pool, b.v_pool, b.block_tables, b.seq_ids,
@@ -597,8 +601,11 @@ def run_decode64(args, rank, world, dist, h):
                                                   b.seq_ids, b.positions, SCALE)
 
     per_step = launches_per_call(step_fn(batches[0]))
+    assert K.last_attention_path() == 4, "the append was not folded into the decode kernel"
     for b in batches[1:]:
         step_fn(b)()
+    for b in batches:
+        two_calls(b)()
     torch.cuda.synchronize()
     assert K.last_attention_path() == 1, "attention did not take the TMA tensor-core path"
     assert K.device_errors(dev) == 0
@@ -608,10 +615,12 @@ def run_decode64(args, rank, world, dist, h):
     time.sleep(0.05)
     steps = [step_fn(b) for b in batches]
     ms, (t0, t1), soak = h.run_steps(steps, args.steps, args.warmup, soak_s=args.soak)
+    ms_two, _, _ = h.run_steps([two_calls(b) for b in batches], args.steps, args.warmup)
     kernel_ms = h.interval_ms([attn_fn(b) for b in batches], min(args.graph_steps, 200))
     isolated_ms = h.per_launch_ms([attn_fn(b) for b in batches], min(args.graph_steps, 200))
     clocks.stop()
     per_rank = rank_times(h, ms, args.steps)
+    ms_two = h.max_over_ranks(ms_two)
     ms = h.max_over_ranks(ms)
     kernel_ms = h.max_over_ranks(kernel_ms)
     isolated_ms = h.max_over_ranks(isolated_ms)
@@ -628,15 +637,20 @@ def run_decode64(args, rank, world, dist, h):
         "warmup": args.warmup, "ms_per_step": ms / args.steps, "higher_is_better": True,
         "scaling": "weak", "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
         "config": {"workload": WORKLOAD, "tokens_per_gpu_step": T,
+                   "step": "kv_append_attention: Cache.write + ragged_attention_direct in one "
+                           "call, the append folded into the decode kernel",
                    "parallelism": f"request-sharded x{world} (LPT by context), no collective",
                    "l2": f"{R} rotating batches of ~{abytes / 1e6:.0f} MB each per GPU (> L2)",
                    "graph": f"{min(args.graph_steps, args.steps)} steps per CUDA graph, every "
                             "graph replayed once before the timed region"},
         "ms_per_step_per_rank": per_rank,
+        "two_calls": {"ms_per_step": ms_two / args.steps,
+                      "value": tokens_all * args.steps / (ms_two / 1e3),
+                      "step": "kv_append then ragged_attention_direct (two calls)"},
         "hbm_tbs": achieved / 1e3,
         "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
                      "frac": achieved / peak, "traffic": traffic_from_profile(),
-                     "kernel": "decode_attention_kernel<128,2,1,2> + merge_partials_kernel<128,2>",
+                     "kernel": "decode_attention_kernel<128,2,1,2> (split-K merge in the grid)",
                      "kernel_us": kernel_ms * 1e3,
                      "kernel_us_kind": "average interval of back-to-back attention calls "
                                        "(CUDA events around one graph of 100 calls)",
@@ -1078,10 +1092,9 @@ def run_tp2long(args, rank, world, dist, h):
                      device=h.dev, pool_pages=pool_pages)
     T = b.tokens
 
-    def step():
-        sb.kv_append(b.k_pool, b.v_pool, b.k_new, b.v_new, b.slots)
-        sb.ragged_attention_direct(b.q, b.k_pool, b.v_pool, b.block_tables, b.seq_ids,
-                                   b.positions, SCALE)
+    def step():  # Cache.write + ragged_attention_direct in one call (append folded in)
+        sb.kv_append_attention(b.k_pool, b.v_pool, b.k_new, b.v_new, b.slots, b.q,
+                               b.block_tables, b.seq_ids, b.positions, SCALE)
 
     per_step = launches_per_call(step)
     torch.cuda.synchronize()
@@ -1148,10 +1161,9 @@ def run_e2e(args, b, dev, h, tokens_all):
     stream = torch.cuda.current_stream(dev)
 
     def calls():
-        sb.kv_append(b.k_pool, b.v_pool, dev_buf["k_new"], dev_buf["v_new"], dev_buf["slots"])
-        return sb.ragged_attention_direct(dev_buf["q"], b.k_pool, b.v_pool,
-                                          dev_buf["block_tables"], dev_buf["seq_ids"],
-                                          dev_buf["positions"], SCALE)
+        return sb.kv_append_attention(b.k_pool, b.v_pool, dev_buf["k_new"], dev_buf["v_new"],
+                                      dev_buf["slots"], dev_buf["q"], dev_buf["block_tables"],
+                                      dev_buf["seq_ids"], dev_buf["positions"], SCALE)
 
     def eager():
         dev_flat.copy_(host_flat, non_blocking=True)
@@ -1192,11 +1204,10 @@ def run_e2e(args, b, dev, h, tokens_all):
             "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
             "ms_per_step": ms / args.e2e_steps,
             "api": "one packed pinned H2D copy into static inputs, replay of a CUDA graph of "
-                   "shardserve_b200.kv_append + ragged_attention_direct, D2H of the output, "
-                   "per-step sync",
+                   "shardserve_b200.kv_append_attention, D2H of the output, per-step sync",
             "eager": {"value": tokens_all * args.e2e_steps / (ms_eager / 1e3), "unit": "tok/s",
                       "ms_per_step": ms_eager / args.e2e_steps,
-                      "api": "same copies, the two calls issued eagerly (torch binding)"}}
+                      "api": "same copies, the call issued eagerly (torch binding)"}}
 
 
 def traffic_from_profile():

@@ -213,6 +213,34 @@ SS_API int ss_ragged_paged_attention(const void* q, const int64_t q_strides[3], 
                               void* workspace, size_t workspace_bytes, void* stream);
 
 /*
+ * Slot-mapped KV append followed by ragged paged attention, in one call: the result of
+ * ss_kv_append(k, v -> k_pool / v_pool at slots) then ss_ragged_paged_attention(...) with
+ * the same arguments, the way the reference model calls them per layer
+ * (cache.write then ragged_attention_direct, shardserve/model.py:32-37).
+ * For decode-only launches (query tokens <= block-table rows) whose k / v rows have unit
+ * stride along head_dim and 16-byte aligned starts (element strides multiples of 8), the
+ * append runs inside the attention kernel: the CTA that loads a page writes the new rows of
+ * its token's sequence that fall in that page before loading it, so no append kernel runs.
+ * This needs slots[t] to be token t's own position in its row,
+ * block_tables[seq, pos // 16] * 16 + pos % 16, as the reference builds them
+ * (runtime.py:38); a slot that is not sets SS_DEVERR_SLOT (the row is still written to its
+ * slot when it lies in the pool, but attention then reads the token's page without it).
+ * Other launches run the append kernel first.  ss_last_attention_path() returns 4 when the
+ * append was folded in.  No counterpart in the reference (it fuses two of its calls).
+ * k, v : bf16 [tokens, kv_heads, head_dim]; slots: [tokens] int32 / int64; the rest as
+ * ss_ragged_paged_attention (k_pool / v_pool are written).
+ */
+SS_API int ss_append_ragged_paged_attention(
+    const void* k, const int64_t k_strides[3], const void* v, const int64_t v_strides[3],
+    const void* slots, int slots_is_int64, const void* q, const int64_t q_strides[3],
+    void* k_pool, const int64_t k_pool_strides[4], void* v_pool, const int64_t v_pool_strides[4],
+    const void* block_tables, const int64_t bt_strides[2], int64_t bt_rows, int64_t bt_cols,
+    int bt_is_int64, const void* query_seq_ids, int seq_ids_is_int64, const void* positions,
+    int positions_is_int64, void* out, const int64_t out_strides[3], int64_t tokens, int heads,
+    int kv_heads, int head_dim, int64_t num_pages, float sm_scale, void* workspace,
+    size_t workspace_bytes, void* stream);
+
+/*
  * ss_ragged_paged_attention without a workspace argument: allocation-free.  No counterpart
  * in the reference; it exists for callers that cannot allocate device memory around the
  * call, such as code being recorded into a CUDA graph (cudaMalloc is illegal during stream
@@ -259,7 +287,8 @@ SS_API int ss_noalloc_fetch_device_errors(int device, int clear, uint32_t* flags
  * Which kernel family the last successful ss_ragged_paged_attention call on this thread
  * used: 1 = TMA/tensor-core split-K kernel, 2 = generic strided kernel (layouts the TMA
  * path cannot describe), 3 = split-K kernel for isolated tokens plus tcgen05 tiles for the
- * chunked-prefill runs, 0 = none yet.  Lets tests assert the fast path really ran.
+ * chunked-prefill runs, 4 = split-K kernel with the KV append folded in
+ * (ss_append_ragged_paged_attention), 0 = none yet.  Lets tests assert the fast path really ran.
  */
 SS_API int ss_last_attention_path(void);
 

@@ -13,6 +13,7 @@ from .kernel import (  # noqa: F401
     SUPPORTED_BLOCK_SIZE,
     SUPPORTED_RAGGED_HEAD_DIMS,
     kv_append,
+    kv_append_attention,
     ragged_attention_direct,
     rope_kv_append,
 )
@@ -21,5 +22,6 @@ from .metadata import DeviceMetadata  # noqa: F401
 
 __all__ = [
     "KernelUnsupported", "SUPPORTED_BLOCK_SIZE", "SUPPORTED_RAGGED_HEAD_DIMS", "kv_append",
+    "kv_append_attention",
     "ragged_attention_direct", "rope_kv_append", "Cache", "DeviceMetadata",
 ]

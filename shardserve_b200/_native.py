@@ -65,6 +65,12 @@ SIGNATURES = {
         ctypes.c_int, _vp, ctypes.c_int, _vp, ctypes.c_int, _vp, _i64p, ctypes.c_int64,
         ctypes.c_int, ctypes.c_int, ctypes.c_int, ctypes.c_int64, ctypes.c_float, _vp,
         ctypes.c_size_t, _vp]),
+    "ss_append_ragged_paged_attention": (ctypes.c_int, [
+        _vp, _i64p, _vp, _i64p, _vp, ctypes.c_int,
+        _vp, _i64p, _vp, _i64p, _vp, _i64p, _vp, _i64p, ctypes.c_int64, ctypes.c_int64,
+        ctypes.c_int, _vp, ctypes.c_int, _vp, ctypes.c_int, _vp, _i64p, ctypes.c_int64,
+        ctypes.c_int, ctypes.c_int, ctypes.c_int, ctypes.c_int64, ctypes.c_float, _vp,
+        ctypes.c_size_t, _vp]),
     "ss_ragged_paged_attention_noalloc": (ctypes.c_int, [
         _vp, _i64p, _vp, _i64p, _vp, _i64p, _vp, _i64p, ctypes.c_int64, ctypes.c_int64,
         ctypes.c_int, _vp, ctypes.c_int, _vp, ctypes.c_int, _vp, _i64p, ctypes.c_int64,
@@ -113,8 +119,8 @@ def strides(seq) -> ctypes.Array:
     return arr
 
 
-_BOUND = ("ss_ragged_paged_attention", "ss_kv_append", "ss_rope_kv_append",
-          "ss_attention_workspace_bytes", "ss_last_error_message")
+_BOUND = ("ss_ragged_paged_attention", "ss_append_ragged_paged_attention", "ss_kv_append",
+          "ss_rope_kv_append", "ss_attention_workspace_bytes", "ss_last_error_message")
 
 
 def ops():

@@ -53,6 +53,15 @@ struct DecodeArgs {
   float* part;   // [2 * G] partial-state slots
   unsigned* gbar;  // grid barrier: arrivals at gbar[0], generation at gbar[32] (workspace
                    // bytes 72..75 and 200..203)
+  // Fused append (decode-only launches; app_k null: none).  The step's new K/V rows k / v
+  // [T, KVH, D] (unit stride along head_dim, rows 16-byte addressable) go to slots[t]; the
+  // CTA that loads a page writes the new rows of its token's sequence that fall in that
+  // page, then loads it, so no separate append kernel runs before the call.
+  const __nv_bfloat16* app_k;
+  const __nv_bfloat16* app_v;
+  long long ak_st, ak_sh, av_st, av_sh;
+  const void* app_slots;
+  int app_slots64;
 };
 
 __device__ __forceinline__ long long ld_index(const void* p, int is64, long long i) {

@@ -440,15 +440,29 @@ int ss_attention_workspace_bytes(int device, int64_t tokens, int heads, int kv_h
   return SS_OK;
 }
 
-int ss_ragged_paged_attention(const void* q, const int64_t q_strides[3], const void* k_pool,
-                              const int64_t k_pool_strides[4], const void* v_pool,
-                              const int64_t v_pool_strides[4], const void* block_tables,
-                              const int64_t bt_strides[2], int64_t bt_rows, int64_t bt_cols,
-                              int bt_is_int64, const void* query_seq_ids, int seq_ids_is_int64,
-                              const void* positions, int positions_is_int64, void* out,
-                              const int64_t out_strides[3], int64_t tokens, int heads,
-                              int kv_heads, int head_dim, int64_t num_pages, float sm_scale,
-                              void* workspace, size_t workspace_bytes, void* stream) {
+}  // extern "C"
+
+namespace {
+
+// The step's new K/V rows of ss_append_ragged_paged_attention.
+struct AppendIn {
+  const void* k;
+  const int64_t* ks;
+  const void* v;
+  const int64_t* vs;
+  const void* slots;
+  int slots64;
+};
+
+int attention_impl(const void* q, const int64_t q_strides[3], const void* k_pool,
+                   const int64_t k_pool_strides[4], const void* v_pool,
+                   const int64_t v_pool_strides[4], const void* block_tables,
+                   const int64_t bt_strides[2], int64_t bt_rows, int64_t bt_cols, int bt_is_int64,
+                   const void* query_seq_ids, int seq_ids_is_int64, const void* positions,
+                   int positions_is_int64, void* out, const int64_t out_strides[3],
+                   int64_t tokens, int heads, int kv_heads, int head_dim, int64_t num_pages,
+                   float sm_scale, void* workspace, size_t workspace_bytes, void* stream,
+                   const AppendIn* app) {
   // Checks of the reference wrapper, kernel.py:28-49 (dtype/device checks live in Python).
   if (head_dim != 64 && head_dim != 128)
     return fail(SS_ERR_INVALID, "ragged q must be [tokens, heads, 64|128], got head_dim %d", head_dim);
@@ -503,6 +517,21 @@ int ss_ragged_paged_attention(const void* q, const int64_t q_strides[3], const v
   // sequence rows) and the layout suits the tile kernel; the decode kernel then takes its
   // wide configuration on half of the SMs so that the tiles start on the other half at once.
   const bool want_prefill = tokens > bt_rows && ss::prefill_supported(a);
+  // The append folds into the decode kernel for decode-only launches whose new rows are
+  // 16-byte addressable; otherwise the append kernel runs first.
+  auto rows16 = [](const void* p, const int64_t* st) {
+    return (reinterpret_cast<uintptr_t>(p) & 15) == 0 && st[2] == 1 && st[1] % 8 == 0 &&
+           st[0] % 8 == 0;
+  };
+  const bool fuse = app && tma_layout && !want_prefill && rows16(app->k, app->ks) &&
+                    rows16(app->v, app->vs);
+  if (app && !fuse) {
+    const int rc = ss_kv_append(app->k, app->ks, app->v, app->vs, const_cast<void*>(k_pool),
+                                k_pool_strides, const_cast<void*>(v_pool), v_pool_strides,
+                                app->slots, app->slots64, tokens, num_pages, kv_heads, head_dim,
+                                workspace, stream);
+    if (rc != SS_OK) return rc;
+  }
   if (tma_layout &&
       ss::decode_geometry(device, tokens, heads, kv_heads, head_dim, want_prefill, &g, &why)) {
     const size_t need = ss::kWsHeader + g.desc_bytes + g.part_bytes;
@@ -534,6 +563,21 @@ int ss_ragged_paged_attention(const void* q, const int64_t q_strides[3], const v
       d.part = reinterpret_cast<float*>(ws + ss::kWsHeader);
       d.desc = reinterpret_cast<int4*>(ws + ss::kWsHeader + g.part_bytes);
       d.gbar = reinterpret_cast<unsigned*>(ws + 72);
+      d.app_k = nullptr;
+      d.app_v = nullptr;
+      d.ak_st = d.ak_sh = d.av_st = d.av_sh = 0;
+      d.app_slots = nullptr;
+      d.app_slots64 = 0;
+      if (fuse) {
+        d.app_k = static_cast<const __nv_bfloat16*>(app->k);
+        d.app_v = static_cast<const __nv_bfloat16*>(app->v);
+        d.ak_st = app->ks[0];
+        d.ak_sh = app->ks[1];
+        d.av_st = app->vs[0];
+        d.av_sh = app->vs[1];
+        d.app_slots = app->slots;
+        d.app_slots64 = app->slots64;
+      }
       e = ss::launch_decode(g, tmK, tmV, d, s);
       if (e != cudaSuccess) return cuda_fail(e, "decode attention launch");
       count_launch();
@@ -542,16 +586,64 @@ int ss_ragged_paged_attention(const void* q, const int64_t q_strides[3], const v
         if (e != cudaSuccess) return cuda_fail(e, "prefill attention launch");
         count_launch();
       }
-      g_last_path = prefill ? 3 : 1;
+      g_last_path = prefill ? 3 : (fuse ? 4 : 1);
       return SS_OK;
     }
   }
   // ---- generic strided path -------------------------------------------------------------
+  if (fuse) {  // the TMA path was not taken after all: append first, then the generic kernel
+    const int rc = ss_kv_append(app->k, app->ks, app->v, app->vs, const_cast<void*>(k_pool),
+                                k_pool_strides, const_cast<void*>(v_pool), v_pool_strides,
+                                app->slots, app->slots64, tokens, num_pages, kv_heads, head_dim,
+                                workspace, stream);
+    if (rc != SS_OK) return rc;
+  }
   e = ss::launch_generic_attention(a, s);
   if (e != cudaSuccess) return cuda_fail(e, "generic attention launch");
   count_launch();
   g_last_path = 2;
   return SS_OK;
+}
+
+}  // namespace
+
+extern "C" {
+
+int ss_ragged_paged_attention(const void* q, const int64_t q_strides[3], const void* k_pool,
+                              const int64_t k_pool_strides[4], const void* v_pool,
+                              const int64_t v_pool_strides[4], const void* block_tables,
+                              const int64_t bt_strides[2], int64_t bt_rows, int64_t bt_cols,
+                              int bt_is_int64, const void* query_seq_ids, int seq_ids_is_int64,
+                              const void* positions, int positions_is_int64, void* out,
+                              const int64_t out_strides[3], int64_t tokens, int heads,
+                              int kv_heads, int head_dim, int64_t num_pages, float sm_scale,
+                              void* workspace, size_t workspace_bytes, void* stream) {
+  return attention_impl(q, q_strides, k_pool, k_pool_strides, v_pool, v_pool_strides,
+                        block_tables, bt_strides, bt_rows, bt_cols, bt_is_int64, query_seq_ids,
+                        seq_ids_is_int64, positions, positions_is_int64, out, out_strides,
+                        tokens, heads, kv_heads, head_dim, num_pages, sm_scale, workspace,
+                        workspace_bytes, stream, nullptr);
+}
+
+int ss_append_ragged_paged_attention(
+    const void* k, const int64_t k_strides[3], const void* v, const int64_t v_strides[3],
+    const void* slots, int slots_is_int64, const void* q, const int64_t q_strides[3],
+    void* k_pool, const int64_t k_pool_strides[4], void* v_pool, const int64_t v_pool_strides[4],
+    const void* block_tables, const int64_t bt_strides[2], int64_t bt_rows, int64_t bt_cols,
+    int bt_is_int64, const void* query_seq_ids, int seq_ids_is_int64, const void* positions,
+    int positions_is_int64, void* out, const int64_t out_strides[3], int64_t tokens, int heads,
+    int kv_heads, int head_dim, int64_t num_pages, float sm_scale, void* workspace,
+    size_t workspace_bytes, void* stream) {
+  if (!k || !v || !slots || !k_strides || !v_strides)
+    return fail(SS_ERR_INVALID, "null pointer argument");
+  if (!finite_nonneg_strides(k_strides, 3) || !finite_nonneg_strides(v_strides, 3))
+    return fail(SS_ERR_INVALID, "negative strides are not supported");
+  const AppendIn app{k, k_strides, v, v_strides, slots, slots_is_int64 ? 1 : 0};
+  return attention_impl(q, q_strides, k_pool, k_pool_strides, v_pool, v_pool_strides,
+                        block_tables, bt_strides, bt_rows, bt_cols, bt_is_int64, query_seq_ids,
+                        seq_ids_is_int64, positions, positions_is_int64, out, out_strides,
+                        tokens, heads, kv_heads, head_dim, num_pages, sm_scale, workspace,
+                        workspace_bytes, stream, &app);
 }
 
 int ss_fetch_device_errors(void* workspace, int clear, uint32_t* flags, void* stream) {

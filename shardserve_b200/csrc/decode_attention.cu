@@ -658,6 +658,16 @@ __global__ void __launch_bounds__(Traits<HD, KVB, NG, PR>::kThreads, Traits<HD, 
       }
       const int seg_end = min(np, p + remaining);
       const bool whole = (p == 0 && seg_end == np);
+      // Fused append: this row's sequence starts its run of new tokens at t_first (tokens of
+      // one sequence are contiguous); pages from the first new position on get their new
+      // rows written before they are loaded.
+      long long t_first = t;
+      int first_new_page = 1 << 30;
+      if (d.app_k) {
+        while (t_first > 0 && ld_index(a.seq, a.seq64, t_first - 1) == ti.seq) --t_first;
+        const long long p_first = ld_index(a.pos, a.pos64, t_first);
+        first_new_page = p_first < 0 ? 0 : static_cast<int>(p_first / kPage);
+      }
       const long long row_start = u - p;
       int nparts = 1, slot = 0, cfirst = 0, late = 0;
       if (!whole) {
@@ -695,6 +705,40 @@ __global__ void __launch_bounds__(Traits<HD, KVB, NG, PR>::kThreads, Traits<HD, 
         const int cnt = min(32, seg_end - pb);
         for (int k = 0; k < cnt; ++k) {
           const int pg = __shfl_sync(0xffffffffu, page_id, k);
+          if (d.app_k && pb + k >= first_new_page && pg >= 0) {
+            // New rows of tokens t_first .. t whose position lies in this page: each lane
+            // moves 16 bytes of K and of V (heads b*KVB .. +KVB), then fences the generic
+            // writes before the page's TMA load (async proxy).  Other CTAs loading the page
+            // write the same bytes themselves.
+            constexpr int kChunks = KVB * HD / 8;  // 16-byte chunks per token and tensor
+            for (long long t2 = t_first; t2 <= t; ++t2) {
+              const long long p2 = ld_index(a.pos, a.pos64, t2);
+              if (p2 < 0 || p2 / kPage != pb + k) continue;
+              const long long slot2 = ld_index(d.app_slots, d.app_slots64, t2);
+              if (slot2 != static_cast<long long>(pg) * kPage + p2 % kPage || slot2 < 0 ||
+                  slot2 >= a.N * kPage) {
+                // Not the token's own position (runtime.py:38 builds slots so): the row
+                // still goes to its slot when that lies in the pool, but this page does not
+                // hold it.
+                if (lane == 0) atomicOr(a.err, SS_DEVERR_SLOT);
+                if (slot2 < 0 || slot2 >= a.N * kPage) continue;
+              }
+              if (lane < kChunks) {
+                const int h = b * KVB + lane / (HD / 8), dd = (lane % (HD / 8)) * 8;
+                const long long sp = slot2 / kPage, sr = slot2 % kPage;
+                const uint4 kv = __ldg(reinterpret_cast<const uint4*>(d.app_k + t2 * d.ak_st +
+                                                                      h * d.ak_sh + dd));
+                const uint4 vv = __ldg(reinterpret_cast<const uint4*>(d.app_v + t2 * d.av_st +
+                                                                      h * d.av_sh + dd));
+                *reinterpret_cast<uint4*>(const_cast<__nv_bfloat16*>(a.kp) + sp * a.k_sn +
+                                          sr * a.k_ss + h * a.k_sh + dd) = kv;
+                *reinterpret_cast<uint4*>(const_cast<__nv_bfloat16*>(a.vp) + sp * a.v_sn +
+                                          sr * a.v_ss + h * a.v_sh + dd) = vv;
+              }
+            }
+            fence_proxy_async_global();
+            __syncwarp();
+          }
           if (lane == 0) {
             if (!mbar_wait(bar_empty + 8 * stage, phase ^ 1)) {
               ok = false;

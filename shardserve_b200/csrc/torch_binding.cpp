@@ -36,6 +36,7 @@ namespace py = pybind11;
 namespace {
 
 decltype(&ss_ragged_paged_attention) p_attention = nullptr;
+decltype(&ss_append_ragged_paged_attention) p_append_attention = nullptr;
 decltype(&ss_kv_append) p_append = nullptr;
 decltype(&ss_rope_kv_append) p_rope = nullptr;
 decltype(&ss_attention_workspace_bytes) p_ws_bytes = nullptr;
@@ -45,7 +46,8 @@ PyObject* g_unsupported = nullptr;  // shardserve_b200.kernel.KernelUnsupported 
 constexpr int64_t kBlockSize = 16;
 
 void require_bound() {
-  if (!p_attention || !p_append || !p_rope || !p_ws_bytes || !p_last_error || !g_unsupported)
+  if (!p_attention || !p_append_attention || !p_append || !p_rope || !p_ws_bytes ||
+      !p_last_error || !g_unsupported)
     throw std::runtime_error("shardserve_b200 torch binding used before bind()");
 }
 
@@ -159,11 +161,19 @@ void* err_word(const at::Device& dev) {
   return it == g_ws->end() ? nullptr : it->second.data_ptr();
 }
 
+// The step's new K/V rows of kv_append_attention (nullptr: plain attention).
+struct NewRows {
+  const at::Tensor* k;
+  const at::Tensor* v;
+  const at::Tensor* slots;
+};
+
+void check_kv(const at::Tensor& k, const at::Tensor& v, int64_t kv_heads, int64_t head_dim);
+
 // ---- ragged_attention_direct (reference shardserve/kernel.py:11-82) -------------------------
-at::Tensor ragged_attention_direct(const at::Tensor& q, const at::Tensor& k_pool,
-                                   const at::Tensor& v_pool, const at::Tensor& block_tables,
-                                   const at::Tensor& query_seq_ids, const at::Tensor& positions,
-                                   double sm_scale) {
+at::Tensor attention_call(const at::Tensor& q, const at::Tensor& k_pool, const at::Tensor& v_pool,
+                          const at::Tensor& block_tables, const at::Tensor& query_seq_ids,
+                          const at::Tensor& positions, double sm_scale, const NewRows* rows) {
   require_bound();
   // Checks and messages of the reference wrapper, kernel.py:28-49.
   if (!q.is_cuda() || q.scalar_type() != at::kBFloat16)
@@ -204,14 +214,59 @@ at::Tensor ragged_attention_direct(const at::Tensor& q, const at::Tensor& k_pool
   const Strides<3> qs(q), os(out);
   const Strides<4> ks(k_pool), vs(v_pool);
   const Strides<2> bs(block_tables);
-  check_rc(p_attention(q.data_ptr(), qs.v, k_pool.data_ptr(), ks.v, v_pool.data_ptr(), vs.v,
-                       block_tables.data_ptr(), bs.v, block_tables.size(0), block_tables.size(1),
-                       bt64, seqs.data_ptr(), seq64, pos.data_ptr(), pos64, out.data_ptr(), os.v,
-                       tokens, heads, kv_heads, head_dim, k_pool.size(0),
-                       static_cast<float>(sm_scale), ws.data_ptr(),
-                       static_cast<size_t>(ws.numel()), stream_of(q.device())),
-           "ss_ragged_paged_attention");
+  if (rows == nullptr) {
+    check_rc(p_attention(q.data_ptr(), qs.v, k_pool.data_ptr(), ks.v, v_pool.data_ptr(), vs.v,
+                         block_tables.data_ptr(), bs.v, block_tables.size(0),
+                         block_tables.size(1), bt64, seqs.data_ptr(), seq64, pos.data_ptr(),
+                         pos64, out.data_ptr(), os.v, tokens, heads, kv_heads, head_dim,
+                         k_pool.size(0), static_cast<float>(sm_scale), ws.data_ptr(),
+                         static_cast<size_t>(ws.numel()), stream_of(q.device())),
+             "ss_ragged_paged_attention");
+    return out;
+  }
+  // kv_append's checks (same messages as kv_append), then the fused call.
+  const at::Tensor& k = *rows->k;
+  const at::Tensor& v = *rows->v;
+  check_kv(k, v, kv_heads, head_dim);
+  if (k.size(0) != tokens) unsupported("k/v must hold one row per query token");
+  const std::pair<const char*, const at::Tensor*> row_devices[] = {
+      {"k", &k}, {"v", &v}, {"slots", rows->slots}};
+  for (const auto& nt : row_devices)
+    if (nt.second->device() != q.device())
+      unsupported(std::string(nt.first) + " must be on " + q.device().str());
+  if (rows->slots->numel() != tokens) unsupported("one slot is required per appended token");
+  const int s64 = index_flag(*rows->slots, "slots");
+  const at::Tensor sl = flat_index(*rows->slots);
+  const Strides<3> kst(k), vst(v);
+  check_rc(p_append_attention(k.data_ptr(), kst.v, v.data_ptr(), vst.v, sl.data_ptr(), s64,
+                              q.data_ptr(), qs.v, k_pool.data_ptr(), ks.v, v_pool.data_ptr(),
+                              vs.v, block_tables.data_ptr(), bs.v, block_tables.size(0),
+                              block_tables.size(1), bt64, seqs.data_ptr(), seq64,
+                              pos.data_ptr(), pos64, out.data_ptr(), os.v, tokens, heads,
+                              kv_heads, head_dim, k_pool.size(0), static_cast<float>(sm_scale),
+                              ws.data_ptr(), static_cast<size_t>(ws.numel()),
+                              stream_of(q.device())),
+           "ss_append_ragged_paged_attention");
   return out;
+}
+
+at::Tensor ragged_attention_direct(const at::Tensor& q, const at::Tensor& k_pool,
+                                   const at::Tensor& v_pool, const at::Tensor& block_tables,
+                                   const at::Tensor& query_seq_ids, const at::Tensor& positions,
+                                   double sm_scale) {
+  return attention_call(q, k_pool, v_pool, block_tables, query_seq_ids, positions, sm_scale,
+                        nullptr);
+}
+
+// Cache.write + ragged_attention_direct in one call (reference model.py:32-37).
+at::Tensor kv_append_attention(const at::Tensor& k_pool, const at::Tensor& v_pool,
+                               const at::Tensor& k, const at::Tensor& v, const at::Tensor& slots,
+                               const at::Tensor& q, const at::Tensor& block_tables,
+                               const at::Tensor& query_seq_ids, const at::Tensor& positions,
+                               double sm_scale) {
+  const NewRows rows{&k, &v, &slots};
+  return attention_call(q, k_pool, v_pool, block_tables, query_seq_ids, positions, sm_scale,
+                        &rows);
 }
 
 // Pool checks shared by kv_append and rope_kv_append.
@@ -325,6 +380,7 @@ void take(const py::dict& addrs, const char* name, F*& slot) {
 
 void bind(const py::dict& addrs, const py::object& unsupported_cls) {
   take(addrs, "ss_ragged_paged_attention", p_attention);
+  take(addrs, "ss_append_ragged_paged_attention", p_append_attention);
   take(addrs, "ss_kv_append", p_append);
   take(addrs, "ss_rope_kv_append", p_rope);
   take(addrs, "ss_attention_workspace_bytes", p_ws_bytes);
@@ -345,6 +401,10 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
         py::arg("query_seq_ids"), py::arg("positions"), py::arg("sm_scale"));
   m.def("kv_append", &kv_append, py::arg("k_pool_layer"), py::arg("v_pool_layer"), py::arg("k"),
         py::arg("v"), py::arg("slots"));
+  m.def("kv_append_attention", &kv_append_attention, py::arg("k_pool_layer"),
+        py::arg("v_pool_layer"), py::arg("k"), py::arg("v"), py::arg("slots"), py::arg("q"),
+        py::arg("block_tables"), py::arg("query_seq_ids"), py::arg("positions"),
+        py::arg("sm_scale"));
   m.def("rope_kv_append", &rope_kv_append, py::arg("q"), py::arg("k"), py::arg("v"),
         py::arg("cos"), py::arg("sin"), py::arg("positions"), py::arg("k_pool_layer"),
         py::arg("v_pool_layer"), py::arg("slots"), py::arg("out") = py::none());

@@ -64,7 +64,8 @@ def device_errors(device, clear: bool = True) -> int:
 
 def last_attention_path() -> int:
     """1 = TMA tensor-core split-K kernel, 2 = generic strided kernel, 3 = split-K kernel
-    plus tcgen05 chunked-prefill tiles, 0 = none yet."""
+    plus tcgen05 chunked-prefill tiles, 4 = split-K kernel with the KV append folded in
+    (kv_append_attention), 0 = none yet."""
     return _native.lib().ss_last_attention_path()
 
 
@@ -97,6 +98,20 @@ def ragged_attention_direct(
     # launch run in the torch binding (csrc/torch_binding.cpp).
     return _native.ops().ragged_attention_direct(q, k_pool_layer, v_pool_layer, block_tables,
                                                  query_seq_ids, positions, sm_scale)
+
+
+def kv_append_attention(k_pool_layer: Any, v_pool_layer: Any, k: Any, v: Any, slots: Any,
+                        q: Any, block_tables: Any, query_seq_ids: Any, positions: Any,
+                        sm_scale: float) -> Any:
+    """`kv_append(k_pool_layer, v_pool_layer, k, v, slots)` then
+    `ragged_attention_direct(q, k_pool_layer, v_pool_layer, block_tables, query_seq_ids,
+    positions, sm_scale)` in one call, as the reference model makes them per layer
+    (cache.write then ragged_attention_direct, model.py:32-37).  For a decode step (one query
+    token per row) the append runs inside the attention kernel; slots must then be each
+    token's own position in its row, as the reference builds them (runtime.py:38).  Other
+    batches run the append kernel first."""
+    return _native.ops().kv_append_attention(k_pool_layer, v_pool_layer, k, v, slots, q,
+                                             block_tables, query_seq_ids, positions, sm_scale)
 
 
 def kv_append(k_pool_layer: Any, v_pool_layer: Any, k: Any, v: Any, slots: Any) -> None:
