@@ -1129,14 +1129,19 @@ __global__ void __launch_bounds__(Traits<HD, KVB, NG, PR>::kThreads, Traits<HD, 
   // descriptors are written: the producer wrote its descriptors before the stage arrivals
   // the consumers waited for).
   const int nactive = static_cast<int>((U + chunk - 1) / chunk);
+  // Merge items go to active CTAs by index (item c of each round to CTA c): a CTA at or past
+  // the item count has none, so it arrives and leaves at once, and its SM slot can take a
+  // CTA of the next call while the others merge.
+  const bool has_items = blockIdx.x < a.T * d.nkvblk * (HD / 32);
   named_bar_sync(1, Tr::kNCW * 32);
   if (tid == 0)
-    ctl->merge_mask = grid_barrier(d.gbar, static_cast<unsigned>(d.G), true) ? 1 : 0;
+    ctl->merge_mask = grid_barrier(d.gbar, static_cast<unsigned>(d.G), has_items) ? 1 : 0;
   named_bar_sync(1, Tr::kNCW * 32);
   // Decode-only shape: the next grid on the stream (an append or attention call) may launch
   // now; its CTAs take SM slots only as this grid's CTAs leave.  (The wide shape released
   // the prefill tiles at its entry; the grid after them is released by the tiles.)
   if constexpr (PR <= 2) griddep_launch_dependents();
+  if (!has_items) return;
   if (!ctl->merge_mask) {
     if (tid == 0) atomicOr(a.err, SS_DEVERR_TIMEOUT);
     return;
