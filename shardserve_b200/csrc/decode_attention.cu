@@ -233,28 +233,29 @@ __device__ __forceinline__ uint32_t slab_addr(uint32_t slab, int g, int kk, int 
   return slab + row * 128 + ((chunk16 ^ (key & 7)) << 4);
 }
 
-// Grid-wide barrier over `n` arrivals, one per CTA.  bar[0] counts this call's arrivals,
-// bar[32] (its own 128-byte line, away from the arrivals) is the generation the waiters
-// poll; both are zero before the first call and the last arrival resets bar[0].  A CTA that
-// has no merge work arrives without waiting (`wait` false).  The arrival is an acq_rel
-// atomic by one thread after a CTA barrier: it releases the CTA's writes (partial states,
-// descriptors) and, for the last arrival, acquires everyone else's; the release store of
-// the new generation hands them on to the waiters.  Returns false if the barrier was not
-// opened within kWaitLimitCycles.
+// Grid-wide barrier over `n` arrivals, one per CTA, on two counters that calls use in turn:
+// bar[0] and bar[16] (different 64-byte halves of the header lines) count arrivals, bar[32]
+// says which one this call uses.  All three are zero before the first call.  An arrival is
+// a release reduction by one thread after a CTA barrier (it releases the CTA's partial
+// states and descriptors; no reply to wait for); waiters poll the counter with acquire
+// loads until all n have arrived, then clear the other counter and point bar[32] at it for
+// the next call (every waiter stores the same values).  The next call reads bar[32] only
+// after its programmatic-launch wait, i.e. after this grid has completed, and CTA 0 always
+// waits, so some CTA always makes the switch.  A CTA without merge work arrives without
+// waiting (`wait` false).  Returns false if the count was not complete within
+// kWaitLimitCycles.
 __device__ bool grid_barrier(unsigned* bar, unsigned n, bool wait) {
-  unsigned* gen_p = bar + 32;
-  const unsigned gen = ld_relaxed_gpu_u32(gen_p);  // read before arriving (ordered by the acq_rel)
-  if (atom_add_acq_rel_gpu_u32(bar, 1u) == n - 1) {
-    st_relaxed_gpu_u32(bar, 0u);
-    st_release_gpu_u32(gen_p, gen + 1u);  // open
-    return true;
-  }
+  const unsigned ph = ld_relaxed_gpu_u32(bar + 32) & 1u;
+  unsigned* cnt = bar + 16 * ph;
+  red_release_gpu_add_u32(cnt, 1u);
   if (!wait) return true;
   const long long start = clock64();
-  while (ld_acquire_gpu_u32(gen_p) == gen) {
+  while (ld_acquire_gpu_u32(cnt) < n) {
     if (clock64() - start > kWaitLimitCycles) return false;
-    __nanosleep(256);
+    __nanosleep(64);
   }
+  st_relaxed_gpu_u32(bar + 16 * (ph ^ 1u), 0u);
+  st_relaxed_gpu_u32(bar + 32, ph ^ 1u);
   return true;
 }
 
@@ -432,7 +433,8 @@ __global__ void __launch_bounds__(Traits<HD, KVB, NG, PR>::kThreads, Traits<HD, 
   auto leave_early = [&]() {
     griddep_wait();
     __syncthreads();
-    if (tid == 0) grid_barrier(d.gbar, static_cast<unsigned>(d.G), false);
+    if (tid == 0 && !grid_barrier(d.gbar, static_cast<unsigned>(d.G), blockIdx.x == 0))
+      atomicOr(a.err, SS_DEVERR_TIMEOUT);
   };
   // Wide shape: the launch carries thousands of prefill tokens, and a scan that loads them
   // token by token (several dependent round trips per pass, several passes) kept the
@@ -1135,17 +1137,18 @@ __global__ void __launch_bounds__(Traits<HD, KVB, NG, PR>::kThreads, Traits<HD, 
   const bool has_items = blockIdx.x < a.T * d.nkvblk * (HD / 32);
   named_bar_sync(1, Tr::kNCW * 32);
   if (tid == 0)
-    ctl->merge_mask = grid_barrier(d.gbar, static_cast<unsigned>(d.G), has_items) ? 1 : 0;
+    ctl->merge_mask =
+        grid_barrier(d.gbar, static_cast<unsigned>(d.G), has_items || blockIdx.x == 0) ? 1 : 0;
   named_bar_sync(1, Tr::kNCW * 32);
   // Decode-only shape: the next grid on the stream (an append or attention call) may launch
   // now; its CTAs take SM slots only as this grid's CTAs leave.  (The wide shape released
   // the prefill tiles at its entry; the grid after them is released by the tiles.)
   if constexpr (PR <= 2) griddep_launch_dependents();
-  if (!has_items) return;
   if (!ctl->merge_mask) {
     if (tid == 0) atomicOr(a.err, SS_DEVERR_TIMEOUT);
     return;
   }
+  if (!has_items) return;
   // The stage ring is idle (every stage was consumed before the kDone stage): merge scratch.
   MergeIn mi;
   mi.desc = d.desc;

@@ -366,6 +366,9 @@ __device__ __forceinline__ unsigned atom_add_acq_rel_gpu_u32(unsigned* p, unsign
                : "memory");
   return old;
 }
+__device__ __forceinline__ void red_release_gpu_add_u32(unsigned* p, unsigned v) {
+  asm volatile("red.release.gpu.global.add.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
 __device__ __forceinline__ unsigned ld_acquire_gpu_u32(const unsigned* p) {
   unsigned v;
   asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
