@@ -542,9 +542,10 @@ int attention_impl(const void* q, const int64_t q_strides[3], const void* k_pool
                         head_dim / 64) &&
         encode_pool_map(&tmV, v_pool, num_pages, kv_heads, head_dim, v_pool_strides, g.kvb,
                         head_dim / 64)) {
-      // Otherwise the split-K kernel computes every token.
+      // Otherwise the split-K kernel computes every token.  Only the wide decode shape
+      // evaluates the run predicate, so tiles run only beside it.
       CUtensorMap tmQ, tmKp, tmVp;
-      const bool prefill = want_prefill &&
+      const bool prefill = want_prefill && g.pr > 2 &&
                            encode_q_map(&tmQ, q, tokens, heads, head_dim, q_strides) &&
                            encode_pool_map(&tmKp, k_pool, num_pages, kv_heads, head_dim,
                                            k_pool_strides, 1, 1) &&

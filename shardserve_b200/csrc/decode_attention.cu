@@ -173,22 +173,26 @@ __device__ __forceinline__ long long block_excl_scan(long long v, Ctl* ctl, long
 
 // Units (pages x KV blocks) a token contributes to this launch; -1 marks a token of this
 // launch without keys (its output row is zeros).
+// kRuns: the launch may hold chunked-prefill runs (the wide shape only); the narrow shape
+// never evaluates the run predicate, which keeps its scan loops out of that kernel's code.
+template <bool kRuns>
 __device__ __forceinline__ long long token_units(const DecodeArgs& d, long long t, bool report,
                                                  int* npages_out) {
   const TokInfo ti = token_info(d.a, t, report);
-  const bool mine = !token_in_long_run(d.a, d.min_run, t, ti.seq);
+  const bool mine = !kRuns || !token_in_long_run(d.a, d.min_run, t, ti.seq);
   const int np = mine ? ti.npages : 0;
   if (npages_out) *npages_out = np;
   if (mine && np == 0) return -1;
   return static_cast<long long>(np) * d.nkvblk;
 }
 
-__device__ void write_zero_token(const AttnArgs& a, long long t) {
+// Out of line (it runs only for tokens without keys) and with plain-value arguments (a
+// reference to the kernel's argument block would put a copy of it on the stack).
+__device__ __noinline__ void write_zero_token(__nv_bfloat16* out, long long o_st, long long o_sh,
+                                              long long o_sd, int H, int D, long long t) {
   const __nv_bfloat16 z = __float2bfloat16(0.f);
-  for (int e = 0; e < a.H * a.D; ++e) {
-    const int h = e / a.D, dd = e % a.D;
-    a.out[t * a.o_st + h * a.o_sh + dd * a.o_sd] = z;
-  }
+  for (int h = 0; h < H; ++h)
+    for (int dd = 0; dd < D; ++dd) out[t * o_st + h * o_sh + dd * o_sd] = z;
 }
 
 // A-operand fragments of Q for S = Q.K^T: rows = query heads h0 .. h0+15 of token t.
@@ -425,7 +429,7 @@ __global__ void __launch_bounds__(Traits<HD, KVB, NG, PR>::kThreads, Traits<HD, 
     // reads the descriptors) may still run: wait for them before writing.
     griddep_wait();
     for (int b = 0; b < d.nkvblk; ++b) d.desc[t * d.nkvblk + b] = make_int4(0, 0, 0, 0);
-    if (u < 0) write_zero_token(a, t);
+    if (u < 0) write_zero_token(a.out, a.o_st, a.o_sh, a.o_sd, a.H, a.D, t);
   };
   long long U = 0, chunk = 0, u0 = 0;
   // A CTA leaving before the streaming phase (no units, or a failed staging copy) still
@@ -536,7 +540,7 @@ __global__ void __launch_bounds__(Traits<HD, KVB, NG, PR>::kThreads, Traits<HD, 
       for (int i = 0; i < ITEMS; ++i) {
         const long long t = base + static_cast<long long>(tid) * ITEMS + i;
         if (t < a.T) {
-          const long long u = token_units(d, t, blockIdx.x == 0, nullptr);
+          const long long u = token_units<(PR > 2)>(d, t, blockIdx.x == 0, nullptr);
           if (u <= 0) note_empty(t, u);
           s += u > 0 ? u : 0;
         }
@@ -553,7 +557,7 @@ __global__ void __launch_bounds__(Traits<HD, KVB, NG, PR>::kThreads, Traits<HD, 
       us[i] = 0;
       nps[i] = 0;
       if (t < a.T) {
-        const long long u = token_units(d, t, a.T <= CH && blockIdx.x == 0, &nps[i]);
+        const long long u = token_units<(PR > 2)>(d, t, a.T <= CH && blockIdx.x == 0, &nps[i]);
         if (a.T <= CH && u <= 0) note_empty(t, u);
         us[i] = u > 0 ? u : 0;
       }
@@ -616,7 +620,7 @@ __global__ void __launch_bounds__(Traits<HD, KVB, NG, PR>::kThreads, Traits<HD, 
     TokInfo ti_first;
     {
       const long long t = r / d.nkvblk;
-      token_units(d, t, false, &np_first);
+      token_units<(PR > 2)>(d, t, false, &np_first);
       const TokInfo ti = token_info(a, t, false);
       ti_first = ti;
       const int idx = p + lane;
@@ -650,7 +654,7 @@ __global__ void __launch_bounds__(Traits<HD, KVB, NG, PR>::kThreads, Traits<HD, 
         np = np_first;
         ti = ti_first;
       } else {
-        token_units(d, t, false, &np);
+        token_units<(PR > 2)>(d, t, false, &np);
         ti = token_info(a, t, false);
       }
       if (p >= np) {
@@ -755,7 +759,7 @@ __global__ void __launch_bounds__(Traits<HD, KVB, NG, PR>::kThreads, Traits<HD, 
               if (!next_known) {
                 for (long long r2 = r + 1; r2 < a.T * d.nkvblk; ++r2) {
                   int np2 = 0;
-                  token_units(d, r2 / d.nkvblk, false, &np2);
+                  token_units<(PR > 2)>(d, r2 / d.nkvblk, false, &np2);
                   if (np2 > 0) {
                     next_row = static_cast<int>(r2);
                     break;
