@@ -195,6 +195,28 @@ __device__ __noinline__ void write_zero_token(__nv_bfloat16* out, long long o_st
     for (int dd = 0; dd < D; ++dd) out[t * o_st + h * o_sh + dd * o_sd] = z;
 }
 
+// A token without units in this launch: clear its split descriptors and, for a decode token
+// without keys, write its zero output row.  Out of line: it runs only for such tokens.
+__device__ __noinline__ void clear_empty_token(int4* desc, int nkvblk, long long t, bool zero,
+                                               __nv_bfloat16* out, long long o_st, long long o_sh,
+                                               long long o_sd, int H, int D) {
+  // The preceding grids (the append, and before it the previous call's merge, which reads
+  // the descriptors) may still run: wait for them before writing.
+  griddep_wait();
+  for (int b = 0; b < nkvblk; ++b) desc[t * nkvblk + b] = make_int4(0, 0, 0, 0);
+  if (zero) write_zero_token(out, o_st, o_sh, o_sd, H, D, t);
+}
+
+// A CTA leaving before the streaming phase (no units, or a failed staging copy) still
+// arrives at the grid barrier, after its descriptor writes, without waiting at it (CTA 0
+// waits).  Out of line, called by every thread of the CTA.
+__device__ bool grid_barrier(unsigned* bar, unsigned n, bool wait);
+__device__ __noinline__ void arrive_and_leave(unsigned* gbar, unsigned n, unsigned* err) {
+  griddep_wait();
+  __syncthreads();
+  if (threadIdx.x == 0 && !grid_barrier(gbar, n, blockIdx.x == 0)) atomicOr(err, SS_DEVERR_TIMEOUT);
+}
+
 // A-operand fragments of Q for S = Q.K^T: rows = query heads h0 .. h0+15 of token t.
 // k-step kk holds {row r, d 16kk+2qd..+1}, {row r, d +8} and, when NG == 2, the same for
 // row r + 8.  Rows >= group are zero.
@@ -202,16 +224,13 @@ template <int HD, int NG>
 __device__ __forceinline__ void load_q_frags(const AttnArgs& a, long long t, int h0, int group,
                                              int lane, uint32_t (&qa)[HD / 16][2 * NG]) {
   const int r = lane >> 2, qd = lane & 3;
+  // The host launches this kernel only for q rows that are 16-byte addressable (unit
+  // head_dim stride, head and token strides multiples of 8, 16-byte aligned base).
   const __nv_bfloat16* qt = a.q + t * a.q_st;
-  const bool pair = (a.q_sd == 1) && ((a.q_sh & 1) == 0) && ((a.q_st & 1) == 0) &&
-                    ((reinterpret_cast<uintptr_t>(a.q) & 3) == 0);
   auto ld2 = [&](int row, int dd) -> uint32_t {
     if (row >= group) return 0u;
     const __nv_bfloat16* p = qt + static_cast<long long>(h0 + row) * a.q_sh;
-    if (pair) return __ldg(reinterpret_cast<const unsigned int*>(p + dd));
-    const unsigned short lo = __bfloat16_as_ushort(p[dd * a.q_sd]);
-    const unsigned short hi = __bfloat16_as_ushort(p[(dd + 1) * a.q_sd]);
-    return static_cast<uint32_t>(lo) | (static_cast<uint32_t>(hi) << 16);
+    return __ldg(reinterpret_cast<const unsigned int*>(p + dd));
   };
 #pragma unroll
   for (int kk = 0; kk < HD / 16; ++kk) {
@@ -420,26 +439,15 @@ __global__ void __launch_bounds__(Traits<HD, KVB, NG, PR>::kThreads, Traits<HD, 
   // ---- prologue: total units, this CTA's range, and its first (row, page) ------------
   // Tokens without units in this launch get their split descriptor cleared (and, for
   // decode tokens without keys, a zero output row) by CTA t % G.
-  constexpr int ITEMS = 4;
+  constexpr int ITEMS = 2;
   constexpr int CH = NT * ITEMS;
   auto note_empty = [&](long long t, long long u) {
     // t < 2^31 (token indices are int in the stage metadata): a 32-bit modulo
     if (static_cast<unsigned>(t) % static_cast<unsigned>(d.G) != blockIdx.x) return;
-    // The preceding grids (the append, and before it the previous call's merge, which
-    // reads the descriptors) may still run: wait for them before writing.
-    griddep_wait();
-    for (int b = 0; b < d.nkvblk; ++b) d.desc[t * d.nkvblk + b] = make_int4(0, 0, 0, 0);
-    if (u < 0) write_zero_token(a.out, a.o_st, a.o_sh, a.o_sd, a.H, a.D, t);
+    clear_empty_token(d.desc, d.nkvblk, t, u < 0, a.out, a.o_st, a.o_sh, a.o_sd, a.H, a.D);
   };
   long long U = 0, chunk = 0, u0 = 0;
-  // A CTA leaving before the streaming phase (no units, or a failed staging copy) still
-  // arrives at the grid barrier, after its descriptor writes, without waiting at it.
-  auto leave_early = [&]() {
-    griddep_wait();
-    __syncthreads();
-    if (tid == 0 && !grid_barrier(d.gbar, static_cast<unsigned>(d.G), blockIdx.x == 0))
-      atomicOr(a.err, SS_DEVERR_TIMEOUT);
-  };
+  auto leave_early = [&]() { arrive_and_leave(d.gbar, static_cast<unsigned>(d.G), a.err); };
   // Wide shape: the launch carries thousands of prefill tokens, and a scan that loads them
   // token by token (several dependent round trips per pass, several passes) kept the
   // tiles waiting ~13 us.  Instead the sequence-id and position arrays are copied whole into
@@ -577,16 +585,21 @@ __global__ void __launch_bounds__(Traits<HD, KVB, NG, PR>::kThreads, Traits<HD, 
       leave_early();
       return;
     }
+    long long f_off = -1, f_t = 0;
+    int f_np = 1;
 #pragma unroll
     for (int i = 0; i < ITEMS; ++i) {
       if (us[i] > 0 && start <= u0 && u0 < start + us[i]) {
-        const long long t = base + static_cast<long long>(tid) * ITEMS + i;
-        const long long off = u0 - start;
-        ctl->r0 = t * d.nkvblk + off / nps[i];
-        ctl->off0 = static_cast<int>(off % nps[i]);
-        ctl->found = 1;
+        f_t = base + static_cast<long long>(tid) * ITEMS + i;
+        f_off = u0 - start;
+        f_np = nps[i];
       }
       start += us[i];
+    }
+    if (f_off >= 0) {  // the thread whose tokens hold unit u0
+      ctl->r0 = f_t * d.nkvblk + f_off / f_np;
+      ctl->off0 = static_cast<int>(f_off % f_np);
+      ctl->found = 1;
     }
     run += total;
     __syncthreads();
@@ -832,8 +845,7 @@ __global__ void __launch_bounds__(Traits<HD, KVB, NG, PR>::kThreads, Traits<HD, 
 
   // Queries of the next segment are copied (cp.async, 16 B) into a per-warp double buffer
   // while the current segment streams, when q rows are 16-byte addressable.
-  const bool q_vec = (a.q_sd == 1) && (a.q_sh % 8 == 0) && (a.q_st % 8 == 0) &&
-                     ((reinterpret_cast<uintptr_t>(a.q) & 15) == 0);
+  constexpr bool q_vec = true;  // q rows are 16-byte addressable (checked by the host)
   uint8_t* qbuf = smem + Tr::kOffQ + warp * 2 * Tr::kQBufBytes;
   int qslot = 0;
   long long staged_row = -1;  // row whose q sits in qbuf[qslot ^ 1]

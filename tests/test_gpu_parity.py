@@ -152,6 +152,30 @@ def test_generic_path_for_non_unit_head_dim_stride(dev):
     check_close(out, want)
 
 
+@pytest.mark.parametrize("name", ["config1_decode", "tp2_decode"])
+def test_generic_path_for_queries_not_16_byte_addressable(dev, name):
+    """The split-K kernel reads q rows as 16-byte vectors; a q view that starts one element
+    into its buffer (or has odd strides) runs on the generic kernel, same results."""
+    inp = cases.build(name)
+    want, _ = load_golden(name)
+    t = to_device(inp, dev)
+    T, H, D = t["q"].shape
+    buf = torch.zeros(T * H * D + 1, dtype=torch.bfloat16, device=dev)
+    q_off = buf[1:].view(T, H, D)
+    q_off.copy_(t["q"])
+    assert q_off.data_ptr() % 16 != 0
+    out = run(inp, t, q=q_off)
+    assert K.last_attention_path() == 2
+    check_close(out, want)
+    odd = torch.zeros(T, H, D + 1, dtype=torch.bfloat16, device=dev)[..., :D]
+    odd.copy_(t["q"])
+    assert odd.stride(1) % 8 != 0
+    t2 = to_device(inp, dev)
+    out2 = run(inp, t2, q=odd)
+    assert K.last_attention_path() == 2
+    check_close(out2, want)
+
+
 def test_repeated_calls_are_bitwise_deterministic(dev):
     """The split-K tickets are reset by each call: a second call reuses the workspace."""
     inp = cases.build("long_decode")
