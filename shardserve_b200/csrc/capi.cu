@@ -512,13 +512,15 @@ int attention_impl(const void* q, const int64_t q_strides[3], const void* k_pool
   // ---- fast path: TMA + tensor-core split-K kernel ------------------------------------
   ss::DecodeGeometry g;
   const char* why = "";
-  // The split-K kernel reads q rows as 16-byte vectors: unit head_dim stride, head and
-  // token strides multiples of 8 elements, 16-byte aligned base (other layouts run on the
-  // generic kernel).
-  const bool q_rows16 = q_strides[2] == 1 && q_strides[1] % 8 == 0 && q_strides[0] % 8 == 0 &&
-                        (reinterpret_cast<uintptr_t>(q) & 15) == 0;
-  const bool tma_layout = q_rows16 && pool_tma_ok(k_pool, k_pool_strides) &&
-                          pool_tma_ok(v_pool, v_pool_strides);
+  // The split-K kernel reads q rows and writes output rows as vectors: unit head_dim
+  // stride, head and token strides multiples of 8 elements, 16-byte aligned base (other
+  // layouts run on the generic kernel).
+  auto rows16_ok = [](const void* p, const int64_t* st) {
+    return st[2] == 1 && st[1] % 8 == 0 && st[0] % 8 == 0 &&
+           (reinterpret_cast<uintptr_t>(p) & 15) == 0;
+  };
+  const bool tma_layout = rows16_ok(q, q_strides) && rows16_ok(out, out_strides) &&
+                          pool_tma_ok(k_pool, k_pool_strides) && pool_tma_ok(v_pool, v_pool_strides);
   // Chunked-prefill tiles when the batch must hold a multi-token run (more query tokens than
   // sequence rows) and the layout suits the tile kernel; the decode kernel then takes its
   // wide configuration on half of the SMs so that the tiles start on the other half at once.

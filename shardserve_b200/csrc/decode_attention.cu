@@ -383,15 +383,9 @@ __device__ __noinline__ void merge_split_rows(const MergeIn d, int cta, int nact
         const float inv = L > 0.f ? 1.f / L : 0.f;
         __nv_bfloat16* op = a.out + t * a.o_st +
                             static_cast<long long>((b * KVB + vr / group) * group + vr % group) * a.o_sh;
-        if (a.o_sd == 1 && (reinterpret_cast<uintptr_t>(op + dcol) & 7) == 0) {
-          *reinterpret_cast<uint2*>(op + dcol) =
-              make_uint2(pack_bf16(o.x * inv, o.y * inv), pack_bf16(o.z * inv, o.w * inv));
-        } else {
-          op[dcol * a.o_sd] = __float2bfloat16(o.x * inv);
-          op[(dcol + 1) * a.o_sd] = __float2bfloat16(o.y * inv);
-          op[(dcol + 2) * a.o_sd] = __float2bfloat16(o.z * inv);
-          op[(dcol + 3) * a.o_sd] = __float2bfloat16(o.w * inv);
-        }
+        // Output rows are 16-byte addressable (checked by the host): one 8-byte store.
+        *reinterpret_cast<uint2*>(op + dcol) =
+            make_uint2(pack_bf16(o.x * inv, o.y * inv), pack_bf16(o.z * inv, o.w * inv));
       }
     }
     named_bar_sync(1, NT);  // the compacted list is rebuilt next round
@@ -1108,8 +1102,8 @@ __global__ void __launch_bounds__(Traits<HD, KVB, NG, PR>::kThreads, Traits<HD, 
 #pragma unroll
               for (int mt = 0; mt < HD / 16; ++mt) {
                 const int dd = mt * 16 + r;
-                o[dd * a.o_sd] = __float2bfloat16(acc[n][mt][c] * inv);
-                o[(dd + 8) * a.o_sd] = __float2bfloat16(acc[n][mt][2 + c] * inv);
+                o[dd] = __float2bfloat16(acc[n][mt][c] * inv);  // unit head_dim stride
+                o[dd + 8] = __float2bfloat16(acc[n][mt][2 + c] * inv);
               }
             }
           }

@@ -661,27 +661,21 @@ __global__ void __launch_bounds__(kThreadsP, 1)
           if (!ok) break;
           tc_fence_after();
           const float inv = lsum > 0.f ? 1.f / lsum : 0.f;
-          const bool vec = mine && a.o_sd == 1 && ((reinterpret_cast<uintptr_t>(op) & 15) == 0);
+          // Output rows are 16-byte addressable (prefill_supported): 16-byte stores.
 #pragma unroll
           for (int c = 0; c < 4; ++c) {
             uint32_t orow[32];
             tmem_ld32(tO + c * 32, orow);
             tmem_wait_ld();
             if (mine) {
-              if (vec) {
 #pragma unroll
-                for (int q8 = 0; q8 < 4; ++q8) {
-                  uint4 v;
-                  v.x = pack_bf16(__uint_as_float(orow[q8 * 8 + 0]) * inv, __uint_as_float(orow[q8 * 8 + 1]) * inv);
-                  v.y = pack_bf16(__uint_as_float(orow[q8 * 8 + 2]) * inv, __uint_as_float(orow[q8 * 8 + 3]) * inv);
-                  v.z = pack_bf16(__uint_as_float(orow[q8 * 8 + 4]) * inv, __uint_as_float(orow[q8 * 8 + 5]) * inv);
-                  v.w = pack_bf16(__uint_as_float(orow[q8 * 8 + 6]) * inv, __uint_as_float(orow[q8 * 8 + 7]) * inv);
-                  *reinterpret_cast<uint4*>(op + c * 32 + q8 * 8) = v;
-                }
-              } else {
-#pragma unroll
-                for (int i = 0; i < 32; ++i)
-                  op[static_cast<long long>(c * 32 + i) * a.o_sd] = __float2bfloat16(__uint_as_float(orow[i]) * inv);
+              for (int q8 = 0; q8 < 4; ++q8) {
+                uint4 v;
+                v.x = pack_bf16(__uint_as_float(orow[q8 * 8 + 0]) * inv, __uint_as_float(orow[q8 * 8 + 1]) * inv);
+                v.y = pack_bf16(__uint_as_float(orow[q8 * 8 + 2]) * inv, __uint_as_float(orow[q8 * 8 + 3]) * inv);
+                v.z = pack_bf16(__uint_as_float(orow[q8 * 8 + 4]) * inv, __uint_as_float(orow[q8 * 8 + 5]) * inv);
+                v.w = pack_bf16(__uint_as_float(orow[q8 * 8 + 6]) * inv, __uint_as_float(orow[q8 * 8 + 7]) * inv);
+                *reinterpret_cast<uint4*>(op + c * 32 + q8 * 8) = v;
               }
             }
           }
@@ -744,7 +738,9 @@ bool prefill_supported(const AttnArgs& a) {
   // scale_log2 > 0: the row max is taken over the unscaled scores.
   return a.D == kHDp && a.group == kGroup && a.q_sd == 1 && (a.q_sh % 8) == 0 &&
          (a.q_st % 8) == 0 && (reinterpret_cast<uintptr_t>(a.q) & 15) == 0 &&
-         a.scale_log2 > 0.f && launch_regs_ok();
+         a.o_sd == 1 && (a.o_sh % 8) == 0 && (a.o_st % 8) == 0 &&
+         (reinterpret_cast<uintptr_t>(a.out) & 15) == 0 && a.scale_log2 > 0.f &&
+         launch_regs_ok();
 }
 
 int prefill_min_run() { return kMinRunP; }

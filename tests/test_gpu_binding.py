@@ -145,3 +145,53 @@ def test_plain_ctypes_binding_matches_the_torch_binding(dev):
     via_torch = sb.ragged_attention_direct(b.q, b.k_pool, b.v_pool, tables, seqs, pos, 128 ** -0.5)
     torch.cuda.synchronize()
     assert torch.equal(via_ctypes, via_torch)
+
+
+def test_output_rows_not_16_byte_addressable_run_on_the_generic_kernel(dev):
+    """The split-K and tile kernels write output rows as vectors; an output view that starts
+    one element into its buffer, or has an odd head stride, goes to the generic kernel
+    through the C ABI, with results within the attention tolerance of the fast path."""
+    import ctypes
+
+    from helpers import MAX_ABS_TOL, MEAN_ABS_TOL
+    from shardserve_b200.workloads import decode_batch
+
+    lib = ctypes.CDLL(_native.LIB_PATH)
+    lib.ss_last_error_message.restype = ctypes.c_char_p
+    I64 = ctypes.c_int64
+
+    def strides(t):
+        return (I64 * t.dim())(*t.stride())
+
+    b = decode_batch([300, 17, 2049, 64, 900], 16, 2, 128, seed=72, device=dev)
+    sb.kv_append(b.k_pool, b.v_pool, b.k_new, b.v_new, b.slots)
+    need = ctypes.c_size_t()
+    assert lib.ss_attention_workspace_bytes(0, I64(5), 16, 2, 128, ctypes.byref(need)) == 0
+    ws = torch.zeros(need.value, dtype=torch.uint8, device=dev)
+    seqs = b.seq_ids.to(torch.int32)
+    pos = b.positions.to(torch.int64)
+    tables = b.block_tables.to(torch.int32)
+    T, H, D = b.q.shape
+
+    def attention(out):
+        rc = lib.ss_ragged_paged_attention(
+            ctypes.c_void_p(b.q.data_ptr()), strides(b.q), ctypes.c_void_p(b.k_pool.data_ptr()),
+            strides(b.k_pool), ctypes.c_void_p(b.v_pool.data_ptr()), strides(b.v_pool),
+            ctypes.c_void_p(tables.data_ptr()), strides(tables), I64(tables.shape[0]),
+            I64(tables.shape[1]), 0, ctypes.c_void_p(seqs.data_ptr()), 0,
+            ctypes.c_void_p(pos.data_ptr()), 1, ctypes.c_void_p(out.data_ptr()), strides(out),
+            I64(T), H, 2, D, I64(b.k_pool.shape[0]), ctypes.c_float(D ** -0.5),
+            ctypes.c_void_p(ws.data_ptr()), ctypes.c_size_t(ws.numel()),
+            ctypes.c_void_p(torch.cuda.current_stream().cuda_stream))
+        assert rc == 0, lib.ss_last_error_message().decode()
+        return lib.ss_last_attention_path()
+
+    fast = torch.empty_like(b.q)
+    assert attention(fast) == 1
+    shifted = torch.zeros(T * H * D + 1, dtype=torch.bfloat16, device=dev)[1:].view(T, H, D)
+    odd = torch.zeros(T, H, D + 1, dtype=torch.bfloat16, device=dev)[..., :D]
+    for out in (shifted, odd):
+        assert attention(out) == 2
+        torch.cuda.synchronize()
+        err = (out.float() - fast.float()).abs()
+        assert err.max().item() <= MAX_ABS_TOL and err.mean().item() <= MEAN_ABS_TOL
