@@ -97,6 +97,7 @@ struct Ctl {
   int off0;      // first page inside r0
   int found;
   int merge_mask;  // the grid barrier opened (1) or timed out (0)
+  int nactive;     // CTAs with units (their merge items), set by the prologue
   unsigned long long stage_bar;  // mbarrier of the staged index arrays (wide shape)
   long long red[32];
 };
@@ -433,8 +434,6 @@ __global__ void __launch_bounds__(Traits<HD, KVB, NG, PR>::kThreads, Traits<HD, 
   // ---- prologue: total units, this CTA's range, and its first (row, page) ------------
   // Tokens without units in this launch get their split descriptor cleared (and, for
   // decode tokens without keys, a zero output row) by CTA t % G.
-  constexpr int ITEMS = 2;
-  constexpr int CH = NT * ITEMS;
   auto note_empty = [&](long long t, long long u) {
     // t < 2^31 (token indices are int in the stage metadata): a 32-bit modulo
     if (static_cast<unsigned>(t) % static_cast<unsigned>(d.G) != blockIdx.x) return;
@@ -533,45 +532,25 @@ __global__ void __launch_bounds__(Traits<HD, KVB, NG, PR>::kThreads, Traits<HD, 
       }
     }
   }
-  long long us[ITEMS];
-  int nps[ITEMS];
-  if (!staged && a.T > CH) {  // large batches: a first pass for the total only
-    for (long long base = 0; base < a.T; base += CH) {
-      long long s = 0;
-#pragma unroll
-      for (int i = 0; i < ITEMS; ++i) {
-        const long long t = base + static_cast<long long>(tid) * ITEMS + i;
-        if (t < a.T) {
-          const long long u = token_units<(PR > 2)>(d, t, blockIdx.x == 0, nullptr);
-          if (u <= 0) note_empty(t, u);
-          s += u > 0 ? u : 0;
-        }
-      }
-      U += block_sum<NT>(s, ctl);
-    }
-  }
-  long long run = 0;
-  for (long long base = 0; base < a.T && !staged; base += CH) {
+  if (!staged) {
+    // Each thread scans a run of consecutive tokens (one for batches up to the CTA's thread
+    // count), the CTA's exclusive scan of the runs' unit counts gives every thread its
+    // first unit, and the thread whose run holds unit u0 records this CTA's first row.
+    const long long per = (a.T + NT - 1) / NT;
+    const long long tb = static_cast<long long>(tid) * per, te = min(a.T, tb + per);
     long long s = 0;
-#pragma unroll
-    for (int i = 0; i < ITEMS; ++i) {
-      const long long t = base + static_cast<long long>(tid) * ITEMS + i;
-      us[i] = 0;
-      nps[i] = 0;
-      if (t < a.T) {
-        const long long u = token_units<(PR > 2)>(d, t, a.T <= CH && blockIdx.x == 0, &nps[i]);
-        if (a.T <= CH && u <= 0) note_empty(t, u);
-        us[i] = u > 0 ? u : 0;
-      }
-      s += us[i];
+#pragma unroll 1
+    for (long long t = tb; t < te; ++t) {
+      const long long u = token_units<(PR > 2)>(d, t, blockIdx.x == 0, nullptr);
+      if (u <= 0) note_empty(t, u);
+      s += u > 0 ? u : 0;
     }
-    long long total;
-    long long start = run + block_excl_scan<NT>(s, ctl, total);
-    if (a.T <= CH) U = total;  // single pass: the scan also gives the total
+    long long start = block_excl_scan<NT>(s, ctl, U);
     long long ctas = d.G;  // CTAs that share the units
     if (PR > 2) {
-      const long long per = max(1, d.wide_per);
-      ctas = min(static_cast<long long>(d.G), max(static_cast<long long>(d.lo_ctas), (U + per - 1) / per));
+      const long long per_cta = max(1, d.wide_per);
+      ctas = min(static_cast<long long>(d.G),
+                 max(static_cast<long long>(d.lo_ctas), (U + per_cta - 1) / per_cta));
     }
     chunk = max((U + ctas - 1) / ctas, static_cast<long long>(kMinChunk));
     u0 = static_cast<long long>(blockIdx.x) * chunk;
@@ -579,25 +558,21 @@ __global__ void __launch_bounds__(Traits<HD, KVB, NG, PR>::kThreads, Traits<HD, 
       leave_early();
       return;
     }
-    long long f_off = -1, f_t = 0;
-    int f_np = 1;
-#pragma unroll
-    for (int i = 0; i < ITEMS; ++i) {
-      if (us[i] > 0 && start <= u0 && u0 < start + us[i]) {
-        f_t = base + static_cast<long long>(tid) * ITEMS + i;
-        f_off = u0 - start;
-        f_np = nps[i];
+    if (start <= u0 && u0 < start + s) {  // this thread's run holds unit u0
+#pragma unroll 1
+      for (long long t = tb; t < te; ++t) {
+        int np = 0;
+        const long long u = token_units<(PR > 2)>(d, t, false, &np);
+        if (u > 0 && start <= u0 && u0 < start + u) {
+          const long long off = u0 - start;
+          ctl->r0 = t * d.nkvblk + off / np;
+          ctl->off0 = static_cast<int>(off % np);
+          ctl->found = 1;
+          break;
+        }
+        start += u > 0 ? u : 0;
       }
-      start += us[i];
     }
-    if (f_off >= 0) {  // the thread whose tokens hold unit u0
-      ctl->r0 = f_t * d.nkvblk + f_off / f_np;
-      ctl->off0 = static_cast<int>(f_off % f_np);
-      ctl->found = 1;
-    }
-    run += total;
-    __syncthreads();
-    if (ctl->found) break;
   }
   __syncthreads();
   if (!ctl->found) {  // cannot happen when u0 < U; uniform across the CTA
@@ -605,6 +580,7 @@ __global__ void __launch_bounds__(Traits<HD, KVB, NG, PR>::kThreads, Traits<HD, 
     return;
   }
   const int n_units = static_cast<int>(min(chunk, U - u0));
+  if (tid == 0) ctl->nactive = static_cast<int>((U + chunk - 1) / chunk);  // read after the stream
   // Order of programmatic-launch operations: every CTA waits for the preceding grid (the
   // KV append) before it lets the next grid (prefill tiles or the split-K merge) start, so
   // a dependent grid that starts reads pool pages the append has finished writing.
@@ -1140,7 +1116,7 @@ __global__ void __launch_bounds__(Traits<HD, KVB, NG, PR>::kThreads, Traits<HD, 
   // 0 .. nactive - 1 when every consumer warp is done (the CTA's partial states and
   // descriptors are written: the producer wrote its descriptors before the stage arrivals
   // the consumers waited for).
-  const int nactive = static_cast<int>((U + chunk - 1) / chunk);
+  const int nactive = ctl->nactive;
   // Merge items go to active CTAs by index (item c of each round to CTA c): a CTA at or past
   // the item count has none, so it arrives and leaves at once, and its SM slot can take a
   // CTA of the next call while the others merge.
