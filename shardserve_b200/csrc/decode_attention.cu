@@ -601,11 +601,19 @@ __global__ void __launch_bounds__(Traits<HD, KVB, NG, PR>::kThreads, Traits<HD, 
     // (after griddepcontrol.wait these loads would miss L1 again).
     int np_first = 0;
     TokInfo ti_first;
+    long long tf_first = 0;  // fused append: the first row's first new token and its page
+    int fnp_first = 1 << 30;
     {
       const long long t = r / d.nkvblk;
       token_units<(PR > 2)>(d, t, false, &np_first);
       const TokInfo ti = token_info(a, t, false);
       ti_first = ti;
+      if (d.app_k) {
+        tf_first = t;
+        while (tf_first > 0 && ld_index(a.seq, a.seq64, tf_first - 1) == ti.seq) --tf_first;
+        const long long p_first = ld_index(a.pos, a.pos64, tf_first);
+        fnp_first = p_first < 0 ? 0 : static_cast<int>(p_first / kPage);
+      }
       const int idx = p + lane;
       if (idx < min(ti.npages, p + remaining)) {
         const long long pid = ld_index(a.bt, a.bt64, ti.seq * a.bt_sb + idx * a.bt_sn);
@@ -652,7 +660,10 @@ __global__ void __launch_bounds__(Traits<HD, KVB, NG, PR>::kThreads, Traits<HD, 
       // rows written before they are loaded.
       long long t_first = t;
       int first_new_page = 1 << 30;
-      if (d.app_k) {
+      if (use_pf) {  // found before the wait
+        t_first = tf_first;
+        first_new_page = fnp_first;
+      } else if (d.app_k) {
         while (t_first > 0 && ld_index(a.seq, a.seq64, t_first - 1) == ti.seq) --t_first;
         const long long p_first = ld_index(a.pos, a.pos64, t_first);
         first_new_page = p_first < 0 ? 0 : static_cast<int>(p_first / kPage);
