@@ -98,6 +98,9 @@ struct Ctl {
   int found;
   int merge_mask;  // the grid barrier opened (1) or timed out (0)
   int nactive;     // CTAs with units (their merge items), set by the prologue
+  int m_np;        // pages of this CTA's merge row (first item), -1: not found by the scan
+  long long m_start;  // first unit of that row
+  long long chunk;    // units per CTA
   unsigned long long stage_bar;  // mbarrier of the staged index arrays (wide shape)
   long long red[32];
 };
@@ -300,7 +303,7 @@ struct MergeIn {  // what the merge reads and writes (plain values: no kernel-pa
 
 template <int HD, int KVB, int NT>
 __device__ __noinline__ void merge_split_rows(const MergeIn d, int cta, int nactive,
-                                              uint8_t* scratch) {
+                                              uint8_t* scratch, bool known, int4 ds_known) {
   constexpr int R = 16 * KVB;       // query-head rows per partial slot
   constexpr int SF = R * (HD + 2);  // floats per slot
   constexpr int NSL = HD / 32;      // slices per row
@@ -319,7 +322,13 @@ __device__ __noinline__ void merge_split_rows(const MergeIn d, int cta, int nact
     if (tid == 0) *nitems = 0;
     named_bar_sync(1, NT);
     const long long w = base + static_cast<long long>(tid) * nactive;
-    if (w < npairs) {
+    if (known) {  // one item, its descriptor computed by the prologue scan
+      if (tid == 0) {
+        items[0] = w;
+        descs[0] = ds_known;
+        *nitems = 1;
+      }
+    } else if (w < npairs) {
       const int4 ds = __ldcg(&d.desc[w / NSL]);
       if (ds.x >= 2) {
         const int k = atomicAdd(nitems, 1);
@@ -418,6 +427,7 @@ __global__ void __launch_bounds__(Traits<HD, KVB, NG, PR>::kThreads, Traits<HD, 
     }
     fence_mbar_init();
     ctl->found = 0;
+    ctl->m_np = -1;
   }
   if (warp == Tr::kNCW && lane == 0) {
     prefetch_tensormap(&tmK);
@@ -538,14 +548,28 @@ __global__ void __launch_bounds__(Traits<HD, KVB, NG, PR>::kThreads, Traits<HD, 
     // first unit, and the thread whose run holds unit u0 records this CTA's first row.
     const long long per = (a.T + NT - 1) / NT;
     const long long tb = static_cast<long long>(tid) * per, te = min(a.T, tb + per);
-    long long s = 0;
+    // This CTA's first merge item is (row c / slices, slice c % slices): its row's unit
+    // range, found by the same scan, spares the merge a descriptor read.
+    const int m_row = static_cast<int>(blockIdx.x) / (HD / 32);
+    const int m_t = m_row / d.nkvblk, m_b = m_row - m_t * d.nkvblk;
+    long long s = 0, m_local = -1;
+    int m_np = 0;
 #pragma unroll 1
     for (long long t = tb; t < te; ++t) {
-      const long long u = token_units<(PR > 2)>(d, t, blockIdx.x == 0, nullptr);
+      int np = 0;
+      const long long u = token_units<(PR > 2)>(d, t, blockIdx.x == 0, &np);
       if (u <= 0) note_empty(t, u);
+      if (t == m_t) {
+        m_local = s;
+        m_np = u > 0 ? np : 0;
+      }
       s += u > 0 ? u : 0;
     }
     long long start = block_excl_scan<NT>(s, ctl, U);
+    if (m_local >= 0) {
+      ctl->m_start = start + m_local + static_cast<long long>(m_b) * m_np;
+      ctl->m_np = m_np;
+    }
     long long ctas = d.G;  // CTAs that share the units
     if (PR > 2) {
       const long long per_cta = max(1, d.wide_per);
@@ -580,7 +604,10 @@ __global__ void __launch_bounds__(Traits<HD, KVB, NG, PR>::kThreads, Traits<HD, 
     return;
   }
   const int n_units = static_cast<int>(min(chunk, U - u0));
-  if (tid == 0) ctl->nactive = static_cast<int>((U + chunk - 1) / chunk);  // read after the stream
+  if (tid == 0) {  // read after the stream
+    ctl->nactive = static_cast<int>((U + chunk - 1) / chunk);
+    ctl->chunk = chunk;
+  }
   // Order of programmatic-launch operations: every CTA waits for the preceding grid (the
   // KV append) before it lets the next grid (prefill tiles or the split-K merge) start, so
   // a dependent grid that starts reads pool pages the append has finished writing.
@@ -1131,7 +1158,22 @@ __global__ void __launch_bounds__(Traits<HD, KVB, NG, PR>::kThreads, Traits<HD, 
   // Merge items go to active CTAs by index (item c of each round to CTA c): a CTA at or past
   // the item count has none, so it arrives and leaves at once, and its SM slot can take a
   // CTA of the next call while the others merge.
-  const bool has_items = blockIdx.x < a.T * d.nkvblk * (HD / 32);
+  const long long npairs = a.T * d.nkvblk * (HD / 32);
+  bool has_items = blockIdx.x < npairs;
+  // At most one item per CTA: its split descriptor follows from the row's unit range; a
+  // row inside one CTA (or without units) needs no merge, and its CTA does not wait.
+  const bool known = has_items && npairs <= nactive && ctl->m_np >= 0;
+  int4 ds_known = make_int4(0, 0, 0, 0);
+  if (known) {
+    const long long ms = ctl->m_start, ch = ctl->chunk;
+    const int mnp = ctl->m_np;
+    if (mnp > 0) {
+      const long long cf = ms / ch, cl = (ms + mnp - 1) / ch;
+      ds_known = make_int4(static_cast<int>(cl - cf + 1), static_cast<int>(cf),
+                           ms != cf * ch ? kFirstPartLate : 0, 0);
+    }
+    has_items = ds_known.x >= 2;
+  }
   named_bar_sync(1, Tr::kNCW * 32);
   if (tid == 0)
     ctl->merge_mask =
@@ -1157,7 +1199,7 @@ __global__ void __launch_bounds__(Traits<HD, KVB, NG, PR>::kThreads, Traits<HD, 
   mi.T = a.T;
   mi.nkvblk = d.nkvblk;
   mi.group = a.group;
-  merge_split_rows<HD, KVB, Tr::kNCW * 32>(mi, blockIdx.x, nactive, smem);
+  merge_split_rows<HD, KVB, Tr::kNCW * 32>(mi, blockIdx.x, nactive, smem, known, ds_known);
 }
 
 
