@@ -80,6 +80,8 @@ def parse():
     p.add_argument("--e2e-steps", type=int, default=200)
     p.add_argument("--cpu-seconds", type=float, default=10.0)
     p.add_argument("--pool-frac", type=float, default=0.6, help="tp2long pool share of HBM")
+    p.add_argument("--layers", type=int, default=36,
+                   help="layers of the layers36 workload (fewer: a smaller case for profiling)")
     p.add_argument("--seed", type=int, default=2024)
     p.add_argument("--no-extras", action="store_true",
                    help="decode64: skip the other configurations attached to the line")
@@ -1016,7 +1018,7 @@ def run_layers36(args, rank, world, dist, h):
     from shardserve_b200.sharding import shard_requests
     from shardserve_b200.workloads import attention_bytes, ragged_batch, uniform_lengths
 
-    layers, hidden = 36, 2048
+    layers, hidden = args.layers, 2048
     lengths = uniform_lengths(256, 512, 8192, args.seed)
     mine = [lengths[i] for i in shard_requests(lengths, world)[rank]]
     b = ragged_batch([(L - 1, 1) for L in mine], HEADS, KV_HEADS, HEAD_DIM, seed=args.seed + rank,
@@ -1057,8 +1059,8 @@ def run_layers36(args, rank, world, dist, h):
     # Per GPU: its own bytes over the slowest rank's step time (all ranks finish the step).
     achieved = abytes / step_s / 1e9
     del b, qs, ks, vs
-    return {"metric": "36-layer decode-step RoPE+append+attention tok/s", "workload":
-            "256 sequences (split over the GPUs), context U[512,8192], 16q/2kv, d128, 36 "
+    return {"metric": f"{layers}-layer decode-step RoPE+append+attention tok/s", "workload":
+            f"256 sequences (split over the GPUs), context U[512,8192], 16q/2kv, d128, {layers} "
             "per-layer pools; per layer fused RoPE (theta 1e6) + append, then attention",
             "value": h.sum_over_ranks(T) / step_s, "unit": "tok/s", "n_gpus": world,
             "steps": k, "warmup": w, "ms_per_step": ms / k, "ms_per_step_per_rank": per_rank,
