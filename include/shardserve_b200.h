@@ -175,9 +175,9 @@ SS_API int ss_ipc_close(void* ptr);
 /*
  * Workspace size (bytes) that ss_ragged_paged_attention needs on `device` for this geometry.
  * Byte 0..3 of the workspace is the device error word (zero it to start clean).  Bytes
- * 64..71 hold the chunked-prefill work counter and bytes 72..75, 136..139 and 200..203 the
- * decode kernel's grid barrier: they must be zero before the first call (a freshly zeroed
- * buffer, or the first 256 bytes zeroed) and every call leaves them consistent.  The rest is scratch that every
+ * 64..71 hold the chunked-prefill work counter and bytes 72..79 the decode kernel's grid
+ * barrier counter: they must be zero before the first call (a freshly zeroed buffer, or the
+ * first 256 bytes zeroed) and every call leaves them consistent.  The rest is scratch that every
  * call rewrites before reading (split-K partial states and per-row split descriptors), so
  * one buffer can be reused across calls on one stream without clearing.  Calls that run
  * concurrently on different streams need different workspaces.

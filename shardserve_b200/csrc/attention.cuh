@@ -51,8 +51,7 @@ struct DecodeArgs {
   int4* desc;    // [T * nkvblk] split descriptor per row: {parts (0 none, 1 whole), first
                  // CTA, first part in the CTA's second slot, 0}; rewritten every call
   float* part;   // [2 * G] partial-state slots
-  unsigned* gbar;  // grid barrier: arrival counters gbar[0] and gbar[16], the one in use
-                   // named by gbar[32] (workspace bytes 72..75, 136..139, 200..203)
+  unsigned* gbar;  // grid barrier: 64-bit arrival counter (workspace bytes 72..79)
   // Fused append (decode-only launches; app_k null: none).  The step's new K/V rows k / v
   // [T, KVH, D] (unit stride along head_dim, rows 16-byte addressable) go to slots[t]; the
   // CTA that loads a page writes the new rows of its token's sequence that fall in that
@@ -238,7 +237,7 @@ cudaError_t launch_tp2_oproj(const CUtensorMap& tmA, const CUtensorMap& tmW, con
 void set_error_message(const char* fmt, ...);
 
 // Workspace layout (fixed per device): [0, 256) header (error word at byte 0, chunked-prefill
-// work counter at bytes 64..71, decode grid barrier at bytes 72..75, 136..139 and 200..203:
+// work counter at bytes 64..71, decode grid barrier counter at bytes 72..79:
 // zero before the first call, left consistent by every call), then the partial-state region
 // (sized for the
 // largest decode kernel instance), then one int4 split descriptor per (token, KV block) row.

@@ -212,13 +212,13 @@ __device__ __noinline__ void clear_empty_token(int4* desc, int nkvblk, long long
 }
 
 // A CTA leaving before the streaming phase (no units, or a failed staging copy) still
-// arrives at the grid barrier, after its descriptor writes, without waiting at it (CTA 0
-// waits).  Out of line, called by every thread of the CTA.
+// arrives at the grid barrier, after its descriptor writes, without waiting at it.  Out of
+// line, called by every thread of the CTA.
 __device__ bool grid_barrier(unsigned* bar, unsigned n, bool wait);
-__device__ __noinline__ void arrive_and_leave(unsigned* gbar, unsigned n, unsigned* err) {
+__device__ __noinline__ void arrive_and_leave(unsigned* gbar, unsigned n) {
   griddep_wait();
   __syncthreads();
-  if (threadIdx.x == 0 && !grid_barrier(gbar, n, blockIdx.x == 0)) atomicOr(err, SS_DEVERR_TIMEOUT);
+  if (threadIdx.x == 0) grid_barrier(gbar, n, false);
 }
 
 // A-operand fragments of Q for S = Q.K^T: rows = query heads h0 .. h0+15 of token t.
@@ -260,29 +260,30 @@ __device__ __forceinline__ uint32_t slab_addr(uint32_t slab, int g, int kk, int 
   return slab + row * 128 + ((chunk16 ^ (key & 7)) << 4);
 }
 
-// Grid-wide barrier over `n` arrivals, one per CTA, on two counters that calls use in turn:
-// bar[0] and bar[16] (different 64-byte halves of the header lines) count arrivals, bar[32]
-// says which one this call uses.  All three are zero before the first call.  An arrival is
-// a release reduction by one thread after a CTA barrier (it releases the CTA's partial
-// states and descriptors; no reply to wait for); waiters poll the counter with acquire
-// loads until all n have arrived, then clear the other counter and point bar[32] at it for
-// the next call (every waiter stores the same values).  The next call reads bar[32] only
-// after its programmatic-launch wait, i.e. after this grid has completed, and CTA 0 always
-// waits, so some CTA always makes the switch.  A CTA without merge work arrives without
-// waiting (`wait` false).  Returns false if the count was not complete within
-// kWaitLimitCycles.
+// Grid-wide barrier over n <= 2^16 arrivals, one per CTA, on a 64-bit counter (workspace
+// bytes 72..79, zero before the first call) that is never reset or stored to: every call adds
+// exactly 2^16 to it (CTA 0 adds 2^16 - (n - 1), every other CTA 1), so the value an arrival
+// returns names its call (old >> 16) and the call's CTAs have all arrived once the counter
+// reaches the next multiple of 2^16.  Arrivals are release additions by one thread after a CTA
+// barrier (they release the CTA's partial states and descriptors); waiters poll with acquire
+// loads.  A CTA without merge work arrives without waiting (`wait` false).  Only additions
+// write the counter, so no write of one call can land on another call's arrivals.  Returns
+// false if the count was not complete within kWaitLimitCycles.
+constexpr unsigned long long kBarrierQuantum = 1ull << 16;
 __device__ bool grid_barrier(unsigned* bar, unsigned n, bool wait) {
-  const unsigned ph = ld_relaxed_gpu_u32(bar + 32) & 1u;
-  unsigned* cnt = bar + 16 * ph;
-  red_release_gpu_add_u32(cnt, 1u);
-  if (!wait) return true;
+  unsigned long long* c = reinterpret_cast<unsigned long long*>(bar);
+  const unsigned long long add = blockIdx.x == 0 ? kBarrierQuantum - (n - 1) : 1ull;
+  if (!wait) {
+    red_release_gpu_add_u64(c, add);
+    return true;
+  }
+  const unsigned long long old = atom_add_acq_rel_gpu_u64(c, add);
+  const unsigned long long target = (old / kBarrierQuantum + 1) * kBarrierQuantum;
   const long long start = clock64();
-  while (ld_acquire_gpu_u32(cnt) < n) {
+  while (ld_acquire_gpu_u64(c) < target) {
     if (clock64() - start > kWaitLimitCycles) return false;
     __nanosleep(64);
   }
-  st_relaxed_gpu_u32(bar + 16 * (ph ^ 1u), 0u);
-  st_relaxed_gpu_u32(bar + 32, ph ^ 1u);
   return true;
 }
 
@@ -450,7 +451,7 @@ __global__ void __launch_bounds__(Traits<HD, KVB, NG, PR>::kThreads, Traits<HD, 
     clear_empty_token(d.desc, d.nkvblk, t, u < 0, a.out, a.o_st, a.o_sh, a.o_sd, a.H, a.D);
   };
   long long U = 0, chunk = 0, u0 = 0;
-  auto leave_early = [&]() { arrive_and_leave(d.gbar, static_cast<unsigned>(d.G), a.err); };
+  auto leave_early = [&]() { arrive_and_leave(d.gbar, static_cast<unsigned>(d.G)); };
   // Wide shape: the launch carries thousands of prefill tokens, and a scan that loads them
   // token by token (several dependent round trips per pass, several passes) kept the
   // tiles waiting ~13 us.  Instead the sequence-id and position arrays are copied whole into
@@ -1177,7 +1178,7 @@ __global__ void __launch_bounds__(Traits<HD, KVB, NG, PR>::kThreads, Traits<HD, 
   named_bar_sync(1, Tr::kNCW * 32);
   if (tid == 0)
     ctl->merge_mask =
-        grid_barrier(d.gbar, static_cast<unsigned>(d.G), has_items || blockIdx.x == 0) ? 1 : 0;
+        grid_barrier(d.gbar, static_cast<unsigned>(d.G), has_items) ? 1 : 0;
   named_bar_sync(1, Tr::kNCW * 32);
   // Decode-only shape: the next grid on the stream (an append or attention call) may launch
   // now; its CTAs take SM slots only as this grid's CTAs leave.  (The wide shape released

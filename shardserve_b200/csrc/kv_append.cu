@@ -5,19 +5,13 @@
 // when both sides are 16-byte addressable along head_dim, else one element.  The copy is
 // bit-exact.
 //
-// Programmatic dependent launch on both sides: the kernel is launched so that it may start
-// while the preceding kernel on the stream finishes (it then waits, griddepcontrol.wait,
-// before it reads k / v or writes the pool), and it releases its dependent grid at entry,
-// so the attention kernel that follows runs its prologue while the append drains; the
-// attention kernel waits for the append before it reads any page.
+// Programmatic dependent launch: the kernel is launched so that it may start while the
+// preceding kernel on the stream finishes (it then waits, griddepcontrol.wait, before it
+// reads k / v or writes the pool).  It does not release the kernel after it early.
 #include <cuda_bf16.h>
 
 #include "attention.cuh"
 #include "ptx.cuh"
-
-#ifndef SS_PDL_APPEND
-#define SS_PDL_APPEND 1
-#endif
 
 namespace ss {
 
@@ -25,7 +19,10 @@ namespace {
 
 template <bool VEC>
 __global__ void __launch_bounds__(256) kv_append_kernel(const AppendArgs a) {
-  griddep_launch_dependents();
+  // The attention kernel after this one is not released early (the kernel ends first): its
+  // grid barrier needs all of its CTAs resident at once, and an SM that still held one of
+  // these CTAs when the attention grid was placed was seen to take only two of the three
+  // attention CTAs it can hold, until it drained.
   griddep_wait();  // k / v may come from the preceding kernel, which may still read the pool
   constexpr int E = VEC ? 8 : 1;  // elements per thread
   const long long per_row = static_cast<long long>(a.KVH) * a.D / E;
@@ -78,7 +75,7 @@ cudaError_t launch_kv_append(const AppendArgs& a, bool vectorised, cudaStream_t 
   attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
   attr[0].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
-  cfg.numAttrs = SS_PDL_APPEND ? 1 : 0;
+  cfg.numAttrs = 1;
   return vectorised ? cudaLaunchKernelEx(&cfg, kv_append_kernel<true>, a)
                     : cudaLaunchKernelEx(&cfg, kv_append_kernel<false>, a);
 }

@@ -37,9 +37,8 @@ __device__ __forceinline__ float bf16r(float x) {
 
 template <bool VEC>
 __global__ void __launch_bounds__(256) rope_append_kernel(const RopeArgs r) {
-  // Programmatic dependent launch both ways (as kv_append_kernel): release the attention
-  // kernel at entry, wait for the preceding kernel before reading q / k / v.
-  griddep_launch_dependents();
+  // Programmatic dependent launch (as kv_append_kernel): may start while the preceding
+  // kernel finishes and waits for it before reading q / k / v; releases nothing early.
   griddep_wait();
   const AppendArgs& a = r.app;
   constexpr int E = VEC ? 8 : 1;  // elements per half (rotation) or per copy (v)

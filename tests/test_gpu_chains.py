@@ -1,0 +1,64 @@
+"""Long chains of calls on one stream, the way a model's layers issue them: RoPE + append
+then attention, append then attention, and the fused append + attention, 200 times each on
+a batch-256 decode step (context U[512, 8192], 16 q / 2 kv heads).
+
+The decode kernel's split-K merge runs after a grid barrier, which needs every CTA of the
+grid resident at once.  An append kernel that released the attention kernel early left SMs
+that could hold only two attention CTAs, and about one call in a hundred waited out the
+barrier's bound (device error SS_DEVERR_TIMEOUT, merge skipped).  These chains check that no
+call of them times out, and that the last call's output equals the same call made alone.
+Reference composition: shardserve/model.py:25-37 (apply_rope, Cache.write, attention).
+"""
+import pytest
+import torch
+
+import shardserve_b200 as sb
+from shardserve_b200 import kernel as K
+from shardserve_b200.workloads import ragged_batch, uniform_lengths
+
+pytestmark = pytest.mark.gpu
+CALLS = 200
+SCALE = 128 ** -0.5
+
+
+@pytest.fixture(scope="module")
+def dev():
+    assert torch.cuda.is_available(), "GPU tests need a CUDA device"
+    return torch.device("cuda", 0)
+
+
+@pytest.fixture(scope="module")
+def batch(dev):
+    lengths = uniform_lengths(256, 512, 8192, 2024)
+    return ragged_batch([(L - 1, 1) for L in lengths], 16, 2, 128, seed=2024, device=dev)
+
+
+def _attention(b, q):
+    return sb.ragged_attention_direct(q, b.k_pool, b.v_pool, b.block_tables, b.seq_ids,
+                                      b.positions, SCALE)
+
+
+@pytest.mark.parametrize("chain", ["rope_append", "kv_append", "fused"])
+def test_long_call_chain_never_times_out(dev, batch, chain):
+    b = batch
+    cos = torch.ones(8192, 128, device=dev)
+    sin = torch.zeros(8192, 128, device=dev)  # identity rotation: q, k unchanged
+    q = b.q.clone()
+    torch.cuda.synchronize()
+    K.device_errors(dev, clear=True)
+    for _ in range(CALLS):
+        if chain == "rope_append":
+            sb.rope_kv_append(q, b.k_new, b.v_new, cos, sin, b.positions, b.k_pool, b.v_pool,
+                              b.slots, out=q)
+            out = _attention(b, q)
+        elif chain == "kv_append":
+            sb.kv_append(b.k_pool, b.v_pool, b.k_new, b.v_new, b.slots)
+            out = _attention(b, q)
+        else:
+            out = sb.kv_append_attention(b.k_pool, b.v_pool, b.k_new, b.v_new, b.slots, q,
+                                         b.block_tables, b.seq_ids, b.positions, SCALE)
+    torch.cuda.synchronize()
+    assert K.device_errors(dev, clear=True) == 0
+    alone = _attention(b, q)
+    torch.cuda.synchronize()
+    assert torch.equal(out, alone)
