@@ -18,10 +18,10 @@
 //    K = 16 keys): P goes from the S accumulators straight into the B operand, so the P.V
 //    product wastes no padded rows and the accumulator is head_dim x 8 per warp.
 //  * A token whose pages span several CTAs leaves fp32 partial (m, l, acc) states.  When
-//    every active CTA has streamed its share (a grid-wide barrier: one arrival per CTA, the
-//    last one opens it; all CTAs of the one-wave grid are resident, no grid that could hold
-//    SM slots is released before it, and every wait is bounded), the same CTAs fold those
-//    states into bf16 outputs, each taking (split row, 32-dim slice) items.  Folding inside
+//    every active CTA has streamed its share (a grid-wide barrier: one arrival per CTA; a
+//    waiter gives up after ~0.5 ms, since a CTA of the grid may not be resident, and the
+//    call's last arrival then merges for it), the same CTAs fold those states into bf16
+//    outputs, each taking (split row, 32- or 64-dim slice) items.  Folding inside
 //    the grid saves a second kernel's launch and CTA dispatch on every call.
 //  * Two CTA shapes.  Decode-only launches: two consumer warps per KV head, 3-4 CTAs per SM
 //    on every SM.  Launches followed by chunked-prefill tiles: the wide CTA (five consumer
@@ -96,7 +96,7 @@ struct Ctl {
   long long r0;  // first row (token * nkvblk + block)
   int off0;      // first page inside r0
   int found;
-  int merge_mask;  // the grid barrier opened (1) or timed out (0)
+  int merge_mask;  // grid_barrier's answer: 0 leave, 1 merge own items, 2 merge every item
   int nactive;     // CTAs with units (their merge items), set by the prologue
   int m_np;        // pages of this CTA's merge row (first item), -1: not found by the scan
   long long m_start;  // first unit of that row
@@ -213,12 +213,16 @@ __device__ __noinline__ void clear_empty_token(int4* desc, int nkvblk, long long
 
 // A CTA leaving before the streaming phase (no units, or a failed staging copy) still
 // arrives at the grid barrier, after its descriptor writes, without waiting at it.  Out of
-// line, called by every thread of the CTA.
-__device__ bool grid_barrier(unsigned* bar, unsigned n, bool wait);
-__device__ __noinline__ void arrive_and_leave(unsigned* gbar, unsigned n) {
+// line, called by every thread of the CTA; returns grid_barrier's answer (2: this arrival
+// completed a call in which CTAs gave up, so this CTA merges every item), shared through
+// `code` in shared memory.
+__device__ int grid_barrier(unsigned* bar, unsigned n, bool wait);
+__device__ __noinline__ int arrive_and_leave(unsigned* gbar, unsigned n, int* code) {
   griddep_wait();
   __syncthreads();
-  if (threadIdx.x == 0) grid_barrier(gbar, n, false);
+  if (threadIdx.x == 0) *code = grid_barrier(gbar, n, false);
+  __syncthreads();
+  return *code;
 }
 
 // A-operand fragments of Q for S = Q.K^T: rows = query heads h0 .. h0+15 of token t.
@@ -260,39 +264,58 @@ __device__ __forceinline__ uint32_t slab_addr(uint32_t slab, int g, int kk, int 
   return slab + row * 128 + ((chunk16 ^ (key & 7)) << 4);
 }
 
-// Grid-wide barrier over n <= 2^16 arrivals, one per CTA, on a 64-bit counter (workspace
-// bytes 72..79, zero before the first call) that is never reset or stored to: every call adds
-// exactly 2^16 to it (CTA 0 adds 2^16 - (n - 1), every other CTA 1), so the value an arrival
-// returns names its call (old >> 16) and the call's CTAs have all arrived once the counter
-// reaches the next multiple of 2^16.  Arrivals are release additions by one thread after a CTA
-// barrier (they release the CTA's partial states and descriptors); waiters poll with acquire
-// loads.  A CTA without merge work arrives without waiting (`wait` false).  Only additions
-// write the counter, so no write of one call can land on another call's arrivals.  Returns
-// false if the count was not complete within kWaitLimitCycles.
+// Grid-wide barrier over n <= 2^16 arrivals, one per CTA, that never waits for a CTA that may
+// not be resident.  Counter: one 64-bit word (workspace bytes 72..79, zero before the first
+// call) changed only by atomic additions.  Bits 0..47 count arrivals: every call adds exactly
+// 2^16 (CTA 0 adds 2^16 - (n - 1), every other CTA 1), so an arrival's old value names its
+// call's start (a multiple of 2^16, modulo 2^48) and the call is complete when the field has
+// grown by 2^16.  Bits 48..63 count give-ups of the current call.  Every arrival is an
+// acq_rel addition by one thread after a CTA barrier (it releases the CTA's partial states and
+// descriptors).  A waiter polls with acquire loads for about 0.5 ms; a CTA of the grid that is
+// not yet resident (another kernel's CTAs can hold its slot) would otherwise keep it waiting
+// for ever, so the waiter then gives up by adding 2^48: if the call completed first, its
+// addition says so and it takes it back and merges as usual; otherwise it leaves, and the
+// arrival that completes the call sees the give-ups in the value it returns, takes them back
+// and merges every item of the call.  A merge writes the same bytes whoever makes it, so an
+// item merged twice is harmless.  Returns 0: leave; 1: merge this CTA's own items; 2: merge
+// every item of the call.
 constexpr unsigned long long kBarrierQuantum = 1ull << 16;
-__device__ bool grid_barrier(unsigned* bar, unsigned n, bool wait) {
+constexpr unsigned long long kGiveUp = 1ull << 48;
+constexpr unsigned long long kArrivalMask = kGiveUp - 1;
+constexpr long long kGiveUpCycles = 1ll << 20;
+__device__ int grid_barrier(unsigned* bar, unsigned n, bool wait) {
   unsigned long long* c = reinterpret_cast<unsigned long long*>(bar);
   const unsigned long long add = blockIdx.x == 0 ? kBarrierQuantum - (n - 1) : 1ull;
-  if (!wait) {
-    red_release_gpu_add_u64(c, add);
-    return true;
-  }
   const unsigned long long old = atom_add_acq_rel_gpu_u64(c, add);
-  const unsigned long long target = (old / kBarrierQuantum + 1) * kBarrierQuantum;
-  const long long start = clock64();
-  while (ld_acquire_gpu_u64(c) < target) {
-    if (clock64() - start > kWaitLimitCycles) return false;
+  const unsigned long long start = old & kArrivalMask & ~(kBarrierQuantum - 1);
+  auto done = [start](unsigned long long v) {
+    return ((v - start) & kArrivalMask) >= kBarrierQuantum;
+  };
+  if (done(old + add)) {  // this arrival completed the call
+    const unsigned long long g = old >> 48;
+    if (g == 0) return wait ? 1 : 0;
+    atom_add_acq_rel_gpu_u64(c, (0ull - g) << 48);
+    return 2;
+  }
+  if (!wait) return 0;
+  const long long t0 = clock64();
+  while (!done(ld_acquire_gpu_u64(c))) {
+    if (clock64() - t0 > kGiveUpCycles) {
+      if (!done(atom_add_acq_rel_gpu_u64(c, kGiveUp))) return 0;
+      atom_add_acq_rel_gpu_u64(c, 0ull - kGiveUp);
+      return 1;
+    }
     __nanosleep(64);
   }
-  return true;
+  return 1;
 }
 
-// Split-K merge after the grid barrier.  Item = (row, 32-dim slice of head_dim); active CTA
+// Split-K merge after the grid barrier.  Item = (row, SD-column slice of head_dim); active CTA
 // c takes items c, c + nactive, ...  A row split over n CTAs left n fp32 partial states
 // (unnormalised O, running max m, running sum l per query head, base 2) in slots 2 (cfirst +
 // p) (+1 for part 0 when the row starts inside CTA cfirst's range).  Per round every thread
 // reads one item's descriptor, the split items are compacted into shared memory, then each
-// thread (valid query-head row, 4 dims) folds up to 8 parts per L2 round trip.  Every read
+// thread (valid query-head row, SD / 8 dims) folds up to 8 parts per L2 round trip.  Every read
 // bypasses L1: the parts come from other SMs during this call.
 struct MergeIn {  // what the merge reads and writes (plain values: no kernel-parameter pointer)
   const int4* desc;
@@ -302,14 +325,15 @@ struct MergeIn {  // what the merge reads and writes (plain values: no kernel-pa
   int nkvblk, group;
 };
 
-template <int HD, int KVB, int NT>
+template <int HD, int KVB, int NT, int SD>
 __device__ __noinline__ void merge_split_rows(const MergeIn d, int cta, int nactive,
                                               uint8_t* scratch, bool known, int4 ds_known) {
   constexpr int R = 16 * KVB;       // query-head rows per partial slot
   constexpr int SF = R * (HD + 2);  // floats per slot
-  constexpr int NSL = HD / 32;      // slices per row
+  constexpr int NSL = HD / SD;      // slices per row
   constexpr int kDirect = 8;        // parts folded from registers per round trip
-  constexpr int RPP = NT / 8;       // rows per pass (8 threads x 4 dims cover 32 dims)
+  constexpr int RPP = NT / 8;       // rows per pass (8 threads cover a slice)
+  constexpr int NV = SD / 32;       // float4 vectors per thread and part (4 or 8 dims)
   const MergeIn& a = d;
   const int tid = threadIdx.x;
   const int group = a.group;
@@ -350,24 +374,29 @@ __device__ __noinline__ void merge_split_rows(const MergeIn d, int cta, int nact
         const int vr = v0 + tid / 8;
         if (vr >= vrows) continue;
         const int srow = (vr / group) * 16 + vr % group;
-        const int dcol = sl * 32 + (tid % 8) * 4;
+        const int dcol = sl * SD + (tid % 8) * (4 * NV);
         float M = -CUDART_INF_F, L = 0.f;
-        float4 o = make_float4(0.f, 0.f, 0.f, 0.f);
+        float4 o[NV];
+#pragma unroll
+        for (int k = 0; k < NV; ++k) o[k] = make_float4(0.f, 0.f, 0.f, 0.f);
         for (int p0 = 0; p0 < nparts; p0 += kDirect) {
           float mv[kDirect], lv[kDirect];
-          float4 vv[kDirect];
+          float4 vv[kDirect][NV];
 #pragma unroll
           for (int u = 0; u < kDirect; ++u) {
             mv[u] = -CUDART_INF_F;
             lv[u] = 0.f;
-            vv[u] = make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll
+            for (int k = 0; k < NV; ++k) vv[u][k] = make_float4(0.f, 0.f, 0.f, 0.f);
             const int pi = p0 + u;
             if (pi < nparts) {
               const float* ps =
                   d.part + static_cast<long long>(2 * (cfirst + pi) + ((pi == 0 && late) ? 1 : 0)) * SF;
               mv[u] = __ldcg(ps + R * HD + srow);
               lv[u] = __ldcg(ps + R * HD + R + srow);
-              vv[u] = __ldcg(reinterpret_cast<const float4*>(ps + srow * HD + dcol));
+#pragma unroll
+              for (int k = 0; k < NV; ++k)
+                vv[u][k] = __ldcg(reinterpret_cast<const float4*>(ps + srow * HD + dcol + 4 * k));
             }
           }
           float Mn = M;
@@ -376,27 +405,35 @@ __device__ __noinline__ void merge_split_rows(const MergeIn d, int cta, int nact
           const float ms = Mn == -CUDART_INF_F ? 0.f : Mn;
           const float sc = ex2(M - ms);
           L *= sc;
-          o.x *= sc;
-          o.y *= sc;
-          o.z *= sc;
-          o.w *= sc;
+#pragma unroll
+          for (int k = 0; k < NV; ++k) {
+            o[k].x *= sc;
+            o[k].y *= sc;
+            o[k].z *= sc;
+            o[k].w *= sc;
+          }
 #pragma unroll
           for (int u = 0; u < kDirect; ++u) {
             const float wgt = ex2(mv[u] - ms);
             L += lv[u] * wgt;
-            o.x += vv[u].x * wgt;
-            o.y += vv[u].y * wgt;
-            o.z += vv[u].z * wgt;
-            o.w += vv[u].w * wgt;
+#pragma unroll
+            for (int k = 0; k < NV; ++k) {
+              o[k].x += vv[u][k].x * wgt;
+              o[k].y += vv[u][k].y * wgt;
+              o[k].z += vv[u][k].z * wgt;
+              o[k].w += vv[u][k].w * wgt;
+            }
           }
           M = Mn;
         }
         const float inv = L > 0.f ? 1.f / L : 0.f;
         __nv_bfloat16* op = a.out + t * a.o_st +
                             static_cast<long long>((b * KVB + vr / group) * group + vr % group) * a.o_sh;
-        // Output rows are 16-byte addressable (checked by the host): one 8-byte store.
-        *reinterpret_cast<uint2*>(op + dcol) =
-            make_uint2(pack_bf16(o.x * inv, o.y * inv), pack_bf16(o.z * inv, o.w * inv));
+        // Output rows are 16-byte addressable (checked by the host): 8-byte stores.
+#pragma unroll
+        for (int k = 0; k < NV; ++k)
+          *reinterpret_cast<uint2*>(op + dcol + 4 * k) =
+              make_uint2(pack_bf16(o[k].x * inv, o[k].y * inv), pack_bf16(o[k].z * inv, o[k].w * inv));
       }
     }
     named_bar_sync(1, NT);  // the compacted list is rebuilt next round
@@ -451,7 +488,30 @@ __global__ void __launch_bounds__(Traits<HD, KVB, NG, PR>::kThreads, Traits<HD, 
     clear_empty_token(d.desc, d.nkvblk, t, u < 0, a.out, a.o_st, a.o_sh, a.o_sd, a.H, a.D);
   };
   long long U = 0, chunk = 0, u0 = 0;
-  auto leave_early = [&]() { arrive_and_leave(d.gbar, static_cast<unsigned>(d.G)); };
+  // What the split-K merge reads and writes (plain values, no kernel-parameter pointer).
+  auto merge_in = [&]() {
+    MergeIn mi;
+    mi.desc = d.desc;
+    mi.part = d.part;
+    mi.out = a.out;
+    mi.o_st = a.o_st;
+    mi.o_sh = a.o_sh;
+    mi.o_sd = a.o_sd;
+    mi.T = a.T;
+    mi.nkvblk = d.nkvblk;
+    mi.group = a.group;
+    return mi;
+  };
+  // Every item of the call, by this CTA alone (items of 64 columns; descriptors from memory).
+  auto merge_all = [&]() {
+    merge_split_rows<HD, KVB, Tr::kNCW * 32, 64>(merge_in(), 0, 1, smem, false,
+                                                 make_int4(0, 0, 0, 0));
+  };
+  auto leave_early = [&]() {
+    if (arrive_and_leave(d.gbar, static_cast<unsigned>(d.G), &ctl->merge_mask) == 2 &&
+        warp < Tr::kNCW)
+      merge_all();
+  };
   // Wide shape: the launch carries thousands of prefill tokens, and a scan that loads them
   // token by token (several dependent round trips per pass, several passes) kept the
   // tiles waiting ~13 us.  Instead the sequence-id and position arrays are copied whole into
@@ -1159,11 +1219,15 @@ __global__ void __launch_bounds__(Traits<HD, KVB, NG, PR>::kThreads, Traits<HD, 
   // Merge items go to active CTAs by index (item c of each round to CTA c): a CTA at or past
   // the item count has none, so it arrives and leaves at once, and its SM slot can take a
   // CTA of the next call while the others merge.
-  const long long npairs = a.T * d.nkvblk * (HD / 32);
+  // Items of 32 head_dim columns when no active CTA would get more than one (the merge is
+  // then one round trip per CTA), else of 64 columns (half as many items, fewer rounds).
+  const long long mrows = a.T * d.nkvblk;
+  const bool items32 = mrows * (HD / 32) <= nactive;
+  const long long npairs = mrows * (items32 ? HD / 32 : HD / 64);
   bool has_items = blockIdx.x < npairs;
   // At most one item per CTA: its split descriptor follows from the row's unit range; a
   // row inside one CTA (or without units) needs no merge, and its CTA does not wait.
-  const bool known = has_items && npairs <= nactive && ctl->m_np >= 0;
+  const bool known = items32 && has_items && ctl->m_np >= 0;
   int4 ds_known = make_int4(0, 0, 0, 0);
   if (known) {
     const long long ms = ctl->m_start, ch = ctl->chunk;
@@ -1176,31 +1240,24 @@ __global__ void __launch_bounds__(Traits<HD, KVB, NG, PR>::kThreads, Traits<HD, 
     has_items = ds_known.x >= 2;
   }
   named_bar_sync(1, Tr::kNCW * 32);
-  if (tid == 0)
-    ctl->merge_mask =
-        grid_barrier(d.gbar, static_cast<unsigned>(d.G), has_items) ? 1 : 0;
+  if (tid == 0) ctl->merge_mask = grid_barrier(d.gbar, static_cast<unsigned>(d.G), has_items);
   named_bar_sync(1, Tr::kNCW * 32);
   // Decode-only shape: the next grid on the stream (an append or attention call) may launch
   // now; its CTAs take SM slots only as this grid's CTAs leave.  (The wide shape released
   // the prefill tiles at its entry; the grid after them is released by the tiles.)
   if constexpr (PR <= 2) griddep_launch_dependents();
-  if (!ctl->merge_mask) {
-    if (tid == 0) atomicOr(a.err, SS_DEVERR_TIMEOUT);
+  const int code = ctl->merge_mask;
+  // The stage ring is idle (every stage was consumed before the kDone stage): merge scratch.
+  if (code == 2) {
+    merge_all();
     return;
   }
-  if (!has_items) return;
-  // The stage ring is idle (every stage was consumed before the kDone stage): merge scratch.
-  MergeIn mi;
-  mi.desc = d.desc;
-  mi.part = d.part;
-  mi.out = a.out;
-  mi.o_st = a.o_st;
-  mi.o_sh = a.o_sh;
-  mi.o_sd = a.o_sd;
-  mi.T = a.T;
-  mi.nkvblk = d.nkvblk;
-  mi.group = a.group;
-  merge_split_rows<HD, KVB, Tr::kNCW * 32>(mi, blockIdx.x, nactive, smem, known, ds_known);
+  if (code == 0 || !has_items) return;
+  const MergeIn mi = merge_in();
+  if (items32)
+    merge_split_rows<HD, KVB, Tr::kNCW * 32, 32>(mi, blockIdx.x, nactive, smem, known, ds_known);
+  else
+    merge_split_rows<HD, KVB, Tr::kNCW * 32, 64>(mi, blockIdx.x, nactive, smem, false, ds_known);
 }
 
 

@@ -19,10 +19,10 @@ namespace {
 
 template <bool VEC>
 __global__ void __launch_bounds__(256) kv_append_kernel(const AppendArgs a) {
-  // The attention kernel after this one is not released early (the kernel ends first): its
-  // grid barrier needs all of its CTAs resident at once, and an SM that still held one of
-  // these CTAs when the attention grid was placed was seen to take only two of the three
-  // attention CTAs it can hold, until it drained.
+  // The attention kernel after this one is not released early (the kernel ends first): an
+  // SM that still held one of these CTAs when the attention grid was placed was seen to take
+  // only two of the three attention CTAs it can hold until it drained, which holds up the
+  // attention kernel's grid barrier.
   griddep_wait();  // k / v may come from the preceding kernel, which may still read the pool
   constexpr int E = VEC ? 8 : 1;  // elements per thread
   const long long per_row = static_cast<long long>(a.KVH) * a.D / E;
