@@ -702,8 +702,9 @@ __global__ void __launch_bounds__(kThreadsP, 1)
       atomicExch(sched + 1, 0u);
     }
   }
-  // This grid completes only after the decode grid before it (programmatic launch chain),
-  // so the merge kernel that waits on this grid also waits on the decode grid.
+  // This grid completes only after the decode grid before it (programmatic launch chain,
+  // the decode grid's split-K merge included), so a kernel that waits on this grid also
+  // waits for every output row of the call.
   griddep_wait();
 }
 
